@@ -1,0 +1,250 @@
+// C-ABI entry points of libh3b.so (declared in include/h3b.h).
+//
+// All kernels live in this one translation unit so they share the device
+// error word.  The host functions validate shapes / alignment, build TMA
+// descriptors, launch on the caller's stream and never synchronize (except
+// h3b_device_error, which is documented to).
+#include <cudaTypedefs.h>
+#include <cuda_fp16.h>
+
+#include <atomic>
+#include <cstdio>
+#include <mutex>
+
+#include "common.cuh"
+#include "quant.cuh"
+#include "gemm_nvfp4.cuh"
+
+namespace h3b {
+
+static std::atomic<long long> g_launches{0};
+
+static inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+static int num_sms() {
+  static int cached[64] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 148;
+  if (dev < 64 && cached[dev]) return cached[dev];
+  int n = 148;
+  cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  if (dev < 64) cached[dev] = n;
+  return n;
+}
+
+static int check_sm100() {
+  int dev = 0, major = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return H3B_ERR_CUDA;
+  if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess)
+    return H3B_ERR_CUDA;
+  return major == 10 ? H3B_OK : H3B_ERR_UNSUPPORTED;
+}
+
+static inline int launched(cudaError_t e) {
+  if (e != cudaSuccess) return H3B_ERR_CUDA;
+  g_launches.fetch_add(1, std::memory_order_relaxed);
+  return H3B_OK;
+}
+
+// ------------------------------------------------------------------ TMA descriptors
+static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+// 2-D u8 tensor [rows, cols_bytes] (row pitch = pitch bytes), box box_cols x box_rows,
+// 128-byte swizzle.
+static int make_tmap_u8_sw128(CUtensorMap* map, const void* base, uint64_t rows,
+                              uint64_t cols_bytes, uint64_t pitch, uint32_t box_cols,
+                              uint32_t box_rows) {
+  auto fn = encode_fn();
+  if (!fn) return H3B_ERR_UNSUPPORTED;
+  cuuint64_t dims[2] = {cols_bytes, rows};
+  cuuint64_t strides[1] = {pitch};
+  cuuint32_t box[2] = {box_cols, box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides,
+                  box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? H3B_OK : H3B_ERR_INVALID_ARG;
+}
+
+}  // namespace h3b
+
+using namespace h3b;
+
+extern "C" {
+
+int h3b_version(void) { return 1; }
+
+const char* h3b_status_string(int s) {
+  switch (s) {
+    case H3B_OK: return "ok";
+    case H3B_ERR_INVALID_ARG: return "invalid argument (shape, size or enum out of range)";
+    case H3B_ERR_ALIGNMENT: return "misaligned pointer or leading dimension";
+    case H3B_ERR_CUDA: return "CUDA runtime error";
+    case H3B_ERR_UNSUPPORTED: return "unsupported device or feature (needs sm_100)";
+    case H3B_ERR_TIMEOUT: return "device-side bounded wait expired";
+    case H3B_ERR_DEVICE: return "device-side failure recorded";
+    default: return "unknown status";
+  }
+}
+
+long long h3b_launch_count(void) { return g_launches.load(std::memory_order_relaxed); }
+
+int h3b_device_error(int* code_out, int clear) {
+  if (!code_out) return H3B_ERR_INVALID_ARG;
+  cudaError_t e = cudaDeviceSynchronize();
+  if (e != cudaSuccess) return H3B_ERR_CUDA;
+  int v = 0;
+  e = cudaMemcpyFromSymbol(&v, g_dev_error, sizeof(int));
+  if (e != cudaSuccess) return H3B_ERR_CUDA;
+  if (clear && v) {
+    const int zero = 0;
+    e = cudaMemcpyToSymbol(g_dev_error, &zero, sizeof(int));
+    if (e != cudaSuccess) return H3B_ERR_CUDA;
+  }
+  *code_out = v;
+  return H3B_OK;
+}
+
+// ------------------------------------------------------------------ quantize
+int h3b_amax_bf16(const void* x, int64_t rows, int64_t cols, int64_t ldx, float* amax_out,
+                  void* stream) {
+  if (!amax_out || rows < 0 || cols < 0 || ldx < cols) return H3B_ERR_INVALID_ARG;
+  if (cols % 8 || ldx % 8) return H3B_ERR_INVALID_ARG;
+  if (!aligned16(x) || (reinterpret_cast<uintptr_t>(amax_out) & 3u)) return H3B_ERR_ALIGNMENT;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  cudaError_t e = cudaMemsetAsync(amax_out, 0, sizeof(float), st);
+  if (e != cudaSuccess) return H3B_ERR_CUDA;
+  const int64_t total = rows * (cols / 8);
+  if (total == 0) return H3B_OK;
+  int64_t blocks = (total + kAmaxThreads * 4 - 1) / (kAmaxThreads * 4);
+  const int64_t cap = (int64_t)num_sms() * 8;
+  if (blocks > cap) blocks = cap;
+  k_amax_bf16<<<(unsigned)blocks, kAmaxThreads, 0, st>>>(
+      static_cast<const __nv_bfloat16*>(x), rows, cols, ldx, amax_out);
+  return launched(cudaGetLastError());
+}
+
+int h3b_nvfp4_quantize(const void* x, int64_t M, int64_t K, int64_t ldx, const float* amax,
+                       float gs_in, float* gs_out, void* q, void* sf, int sf_layout, int64_t Mpad,
+                       void* stream) {
+  if (M < 0 || K <= 0 || K % 64 || ldx < K || ldx % 8 || Mpad < M) return H3B_ERR_INVALID_ARG;
+  if (sf_layout != H3B_SF_ROWMAJOR && sf_layout != H3B_SF_SWIZZLED) return H3B_ERR_INVALID_ARG;
+  if (sf_layout == H3B_SF_SWIZZLED && Mpad % 128) return H3B_ERR_INVALID_ARG;
+  if (!amax && !(gs_in > 0.f)) return H3B_ERR_INVALID_ARG;
+  if (!q || !sf || (M > 0 && !x)) return H3B_ERR_INVALID_ARG;
+  if ((M > 0 && !aligned16(x)) || (reinterpret_cast<uintptr_t>(q) & 3u)) return H3B_ERR_ALIGNMENT;
+  const int64_t total = Mpad * (K / 8);
+  if (total == 0) return H3B_OK;
+  const int64_t per_block = (int64_t)kQuantThreads * kQuantUnroll;
+  int64_t blocks = (total + per_block - 1) / per_block;
+  const int64_t cap = (int64_t)num_sms() * 8;
+  if (blocks > cap) blocks = cap;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  auto xp = static_cast<const __nv_bfloat16*>(x);
+  auto qp = static_cast<uint8_t*>(q);
+  auto sp = static_cast<uint8_t*>(sf);
+  if (sf_layout == H3B_SF_SWIZZLED)
+    k_nvfp4_quantize<H3B_SF_SWIZZLED><<<(unsigned)blocks, kQuantThreads, 0, st>>>(
+        xp, M, K, ldx, amax, gs_in, gs_out, qp, sp, Mpad);
+  else
+    k_nvfp4_quantize<H3B_SF_ROWMAJOR><<<(unsigned)blocks, kQuantThreads, 0, st>>>(
+        xp, M, K, ldx, amax, gs_in, gs_out, qp, sp, Mpad);
+  return launched(cudaGetLastError());
+}
+
+int h3b_nvfp4_dequantize(const void* q, const void* sf, int sf_layout, int64_t sf_rows,
+                         const float* gs, int64_t M, int64_t K, void* out, void* stream) {
+  if (M < 0 || K <= 0 || K % 64 || sf_rows < M) return H3B_ERR_INVALID_ARG;
+  if (sf_layout != H3B_SF_ROWMAJOR && sf_layout != H3B_SF_SWIZZLED) return H3B_ERR_INVALID_ARG;
+  if (sf_layout == H3B_SF_SWIZZLED && sf_rows % 128) return H3B_ERR_INVALID_ARG;
+  if (M == 0) return H3B_OK;
+  if (!q || !sf || !out) return H3B_ERR_INVALID_ARG;
+  if ((reinterpret_cast<uintptr_t>(q) & 3u) || !aligned16(out)) return H3B_ERR_ALIGNMENT;
+  const int64_t total = M * (K / 8);
+  int64_t blocks = (total + 255) / 256;
+  const int64_t cap = (int64_t)num_sms() * 16;
+  if (blocks > cap) blocks = cap;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  auto qp = static_cast<const uint8_t*>(q);
+  auto sp = static_cast<const uint8_t*>(sf);
+  auto op = static_cast<__nv_bfloat16*>(out);
+  if (sf_layout == H3B_SF_SWIZZLED)
+    k_nvfp4_dequantize<H3B_SF_SWIZZLED><<<(unsigned)blocks, 256, 0, st>>>(qp, sp, gs, M, K, op);
+  else
+    k_nvfp4_dequantize<H3B_SF_ROWMAJOR><<<(unsigned)blocks, 256, 0, st>>>(qp, sp, gs, M, K, op);
+  return launched(cudaGetLastError());
+}
+
+// ------------------------------------------------------------------ GEMM
+int h3b_nvfp4_gemm(const void* A, const void* sfA, const float* gsA, int64_t M, int64_t a_rows,
+                   const void* B, const void* sfB, const float* gsB, int64_t gsb_seg, int64_t N,
+                   int64_t K, const void* bias, const void* residual, int64_t ldr, int act,
+                   void* D, int64_t ldd, float* amax_out, void* stream) {
+  if (M < 0 || N <= 0 || K <= 0) return H3B_ERR_INVALID_ARG;
+  if (gsb_seg < 0 || (gsb_seg && (gsb_seg % 128 || N % gsb_seg))) return H3B_ERR_INVALID_ARG;
+  if (K % gemm::KB_ELEMS || N % 128 || a_rows % 128 || a_rows < M) return H3B_ERR_INVALID_ARG;
+  if (ldd < N || ldd % 8) return H3B_ERR_INVALID_ARG;
+  if (residual && (ldr < N || ldr % 8)) return H3B_ERR_INVALID_ARG;
+  if (act != H3B_ACT_NONE && act != H3B_ACT_GELU_TANH) return H3B_ERR_INVALID_ARG;
+  if (M > (int64_t)INT32_MAX - 256 || N > (int64_t)INT32_MAX || K > (int64_t)INT32_MAX)
+    return H3B_ERR_INVALID_ARG;
+  if (M == 0) return H3B_OK;
+  if (!A || !sfA || !B || !sfB || !D) return H3B_ERR_INVALID_ARG;
+  if (!aligned16(A) || !aligned16(B) || !aligned16(sfA) || !aligned16(sfB) || !aligned16(D) ||
+      (bias && !aligned16(bias)) || (residual && !aligned16(residual)))
+    return H3B_ERR_ALIGNMENT;
+  int st0 = check_sm100();
+  if (st0 != H3B_OK) return st0;
+
+  static std::once_flag attr_once;
+  static cudaError_t attr_err = cudaSuccess;
+  std::call_once(attr_once, [] {
+    attr_err = cudaFuncSetAttribute(gemm::k_gemm_nvfp4,
+                                    cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    gemm::SMEM_BYTES);
+  });
+  if (attr_err != cudaSuccess) return H3B_ERR_CUDA;
+
+  gemm::Args args;
+  memset(&args, 0, sizeof(args));
+  int rc = make_tmap_u8_sw128(&args.tmap_a, A, (uint64_t)a_rows, (uint64_t)(K / 2),
+                              (uint64_t)(K / 2), gemm::KB_BYTES, gemm::BM);
+  if (rc != H3B_OK) return rc;
+  rc = make_tmap_u8_sw128(&args.tmap_b, B, (uint64_t)N, (uint64_t)(K / 2), (uint64_t)(K / 2),
+                          gemm::KB_BYTES, gemm::BN);
+  if (rc != H3B_OK) return rc;
+  args.sfa = static_cast<const uint8_t*>(sfA);
+  args.sfb = static_cast<const uint8_t*>(sfB);
+  args.gs_a = gsA;
+  args.gs_b = gsB;
+  args.bias = static_cast<const __nv_bfloat16*>(bias);
+  args.residual = static_cast<const __nv_bfloat16*>(residual);
+  args.d = static_cast<__nv_bfloat16*>(D);
+  args.amax_out = amax_out;
+  args.ldr = residual ? ldr : 0;
+  args.ldd = ldd;
+  args.M = (int)M;
+  args.N = (int)N;
+  args.K = (int)K;
+  args.sf_atoms_k = (int)(K / 64);
+  args.act = act;
+  args.gsb_seg = (int)gsb_seg;
+  dim3 grid((unsigned)((N + gemm::BN - 1) / gemm::BN), (unsigned)((M + gemm::BM - 1) / gemm::BM));
+  gemm::k_gemm_nvfp4<<<grid, gemm::THREADS, gemm::SMEM_BYTES, static_cast<cudaStream_t>(stream)>>>(
+      args);
+  return launched(cudaGetLastError());
+}
+
+}  // extern "C"

@@ -1,0 +1,145 @@
+"""Tensor-level wrappers over the C ABI (torch owns the memory, the kernels
+run on the current CUDA stream).
+
+These are the building blocks the reference-shaped API in ``nvfp4.py`` and
+the row shims in ``kernels/`` are written with.  Every function checks
+dtype / device / contiguity on the host and raises on a non-zero status.
+"""
+from __future__ import annotations
+
+import torch
+
+from . import _lib
+
+SF_ROWMAJOR = 0
+SF_SWIZZLED = 1
+ACT_NONE = 0
+ACT_GELU_TANH = 1
+M_ALIGN = 128
+
+
+def _p(t: torch.Tensor | None):
+    return None if t is None else t.data_ptr()
+
+
+def _stream(dev: torch.device) -> int:
+    return torch.cuda.current_stream(dev).cuda_stream
+
+
+def _need_cuda(*ts: torch.Tensor | None) -> torch.device:
+    dev = None
+    for t in ts:
+        if t is None:
+            continue
+        if not t.is_cuda:
+            raise ValueError("h3b ops take CUDA tensors (there is no CPU path)")
+        if dev is None:
+            dev = t.device
+        elif t.device != dev:
+            raise ValueError(f"tensors on different devices: {dev} vs {t.device}")
+    assert dev is not None
+    return dev
+
+
+def pad_m(m: int) -> int:
+    return ((m + M_ALIGN - 1) // M_ALIGN) * M_ALIGN
+
+
+def swizzled_sf_bytes(rows: int, k: int) -> int:
+    """Bytes of a swizzled scale buffer for ``rows`` x ``k`` values (rows padded to 128)."""
+    return pad_m(rows) * (k // 16)
+
+
+def amax(x: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    """fp32 ``[1]`` tensor = max |x| (bf16 ``x``, last dim contiguous)."""
+    dev = _need_cuda(x)
+    if x.dtype != torch.bfloat16:
+        raise TypeError("amax expects bf16")
+    x2 = x.reshape(-1, x.shape[-1]) if x.dim() != 2 else x
+    if x2.stride(-1) != 1:
+        x2 = x2.contiguous()
+    if out is None:
+        out = torch.empty(1, dtype=torch.float32, device=dev)
+    _lib.check(_lib.lib().h3b_amax_bf16(_p(x2), x2.shape[0], x2.shape[1], x2.stride(0), _p(out),
+                                        _stream(dev)), "h3b_amax_bf16")
+    return out
+
+
+def quantize(x: torch.Tensor, *, mpad: int | None = None, layout: int = SF_SWIZZLED,
+             amax_t: torch.Tensor | None = None, gs: float | None = None,
+             q_out: torch.Tensor | None = None, sf_out: torch.Tensor | None = None,
+             gs_out: torch.Tensor | None = None):
+    """bf16 ``[M, K]`` -> (q u8 ``[Mpad, K/2]``, sf u8 (layout), gs fp32 ``[1]``).
+
+    The global scale comes from ``gs`` when given (``gs=1.0`` is the
+    reference's two-level scheme), else from ``amax_t`` (a device scalar some
+    producer already reduced), else from an amax pass over ``x``.
+    """
+    dev = _need_cuda(x)
+    if x.dtype != torch.bfloat16:
+        raise TypeError("quantize expects bf16")
+    x2 = x.reshape(-1, x.shape[-1]) if x.dim() != 2 else x
+    if x2.stride(-1) != 1 or x2.stride(0) % 8:
+        x2 = x2.contiguous()
+    M, K = x2.shape
+    Mp = M if mpad is None else int(mpad)
+    if layout == SF_SWIZZLED and Mp % M_ALIGN:
+        Mp = pad_m(Mp)
+    if q_out is None:
+        q_out = torch.empty(Mp, K // 2, dtype=torch.uint8, device=dev)
+    if sf_out is None:
+        sf_out = torch.empty(Mp * (K // 16), dtype=torch.uint8, device=dev)
+    if gs_out is None:
+        gs_out = torch.empty(1, dtype=torch.float32, device=dev)
+    if q_out.numel() < Mp * (K // 2) or sf_out.numel() < Mp * (K // 16):
+        raise ValueError("output buffers too small")
+    if gs is None and amax_t is None:
+        amax_t = amax(x2)
+    lib = _lib.lib()
+    st = lib.h3b_nvfp4_quantize(_p(x2), M, K, x2.stride(0), _p(amax_t) if gs is None else None,
+                                float(gs if gs is not None else 0.0), _p(gs_out), _p(q_out),
+                                _p(sf_out), layout, Mp, _stream(dev))
+    _lib.check(st, "h3b_nvfp4_quantize")
+    return q_out, sf_out, gs_out
+
+
+def dequantize(q: torch.Tensor, sf: torch.Tensor, gs: torch.Tensor | None, M: int, K: int, *,
+               layout: int = SF_SWIZZLED, sf_rows: int | None = None,
+               out: torch.Tensor | None = None) -> torch.Tensor:
+    dev = _need_cuda(q, sf, gs)
+    rows = sf_rows if sf_rows is not None else (q.shape[0] if q.dim() == 2 else M)
+    if out is None:
+        out = torch.empty(M, K, dtype=torch.bfloat16, device=dev)
+    st = _lib.lib().h3b_nvfp4_dequantize(_p(q), _p(sf), layout, rows, _p(gs), M, K, _p(out),
+                                         _stream(dev))
+    _lib.check(st, "h3b_nvfp4_dequantize")
+    return out
+
+
+def gemm(qa: torch.Tensor, sfa: torch.Tensor, gsa: torch.Tensor | None, M: int,
+         qb: torch.Tensor, sfb: torch.Tensor, gsb: torch.Tensor | None, N: int, K: int, *,
+         gsb_seg: int = 0, bias: torch.Tensor | None = None,
+         residual: torch.Tensor | None = None, act: int = ACT_NONE,
+         out: torch.Tensor | None = None, amax_out: torch.Tensor | None = None) -> torch.Tensor:
+    """``out[M, N] = epilogue(gsa*gsb * deq(qa) @ deq(qb)^T)`` in bf16.
+
+    ``qa``: u8 ``[a_rows, K/2]`` (a_rows % 128 == 0) with swizzled ``sfa``;
+    ``qb``: u8 ``[N, K/2]`` with swizzled ``sfb``.  ``amax_out`` (fp32 [1],
+    zeroed by the caller) receives max |out| for a following re-quantization.
+    """
+    dev = _need_cuda(qa, sfa, gsa, qb, sfb, gsb, bias, residual, out, amax_out)
+    if qa.dtype != torch.uint8 or qb.dtype != torch.uint8:
+        raise TypeError("packed operands must be uint8")
+    a_rows = qa.shape[0]
+    if out is None:
+        out = torch.empty(M, N, dtype=torch.bfloat16, device=dev)
+    if bias is not None and (bias.dtype != torch.bfloat16 or bias.numel() != N):
+        raise ValueError("bias must be bf16 [N]")
+    if residual is not None and (residual.dtype != torch.bfloat16 or residual.stride(-1) != 1):
+        raise ValueError("residual must be bf16 with a contiguous last dim")
+    ldr = residual.stride(0) if residual is not None else 0
+    st = _lib.lib().h3b_nvfp4_gemm(_p(qa), _p(sfa), _p(gsa), M, a_rows, _p(qb), _p(sfb),
+                                   _p(gsb), gsb_seg, N, K, _p(bias), _p(residual), ldr, act,
+                                   _p(out), out.stride(0), _p(amax_out), _stream(dev))
+    _lib.check(st, "h3b_nvfp4_gemm")
+    return out

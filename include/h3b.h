@@ -1,0 +1,114 @@
+/*
+ * h3b -- C ABI of the B200 (sm_100a) NVFP4 hot path of the h3-engine DiT.
+ *
+ * Every pointer argument is a DEVICE pointer unless stated otherwise; `stream`
+ * is a cudaStream_t passed as void*.  Calls are asynchronous on `stream`,
+ * allocate no device memory, do not synchronize the host, and return an
+ * h3b_status.  Shapes are validated on the host before any launch; a kernel
+ * that detects a fault at run time (a bounded wait that ran out) records it
+ * in a per-device error word, read with h3b_device_error().
+ *
+ * Reference interfaces these entry points replace are cited per function as
+ * h3_inference/<file>:<line> (shauray8/h3-engine).
+ */
+#ifndef H3B_H_
+#define H3B_H_
+
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define H3B_API __attribute__((visibility("default")))
+#else
+#define H3B_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum {
+  H3B_OK = 0,
+  H3B_ERR_INVALID_ARG = 1,   /* a shape, size or enum value is out of range        */
+  H3B_ERR_ALIGNMENT = 2,     /* a pointer or leading dimension is misaligned       */
+  H3B_ERR_CUDA = 3,          /* a CUDA runtime call failed                         */
+  H3B_ERR_UNSUPPORTED = 4,   /* device is not sm_100 or a feature is unavailable   */
+  H3B_ERR_TIMEOUT = 5,       /* device side: a bounded wait expired               */
+  H3B_ERR_DEVICE = 6         /* device side: other recorded failure               */
+} h3b_status;
+
+/* Scale-factor layouts. */
+enum { H3B_SF_ROWMAJOR = 0,  /* e4m3 [rows, K/16], row-major                                   */
+       H3B_SF_SWIZZLED = 1   /* 128x4 tiles of 512 B: (r,c) at ((r/128)*(C/4)+c/4)*512
+                                + (r%32)*16 + ((r%128)/32)*4 + c%4 (C = K/16)                   */
+};
+
+/* GEMM epilogue activations. */
+enum { H3B_ACT_NONE = 0, H3B_ACT_GELU_TANH = 1 };
+
+/* ------------------------------------------------------------------ library */
+H3B_API int h3b_version(void);
+H3B_API const char* h3b_status_string(int status);
+/* Number of kernels this library has launched in this process (all devices). */
+H3B_API long long h3b_launch_count(void);
+/* Reads (and with clear != 0 resets) the current device's error word.
+   Synchronizes the device.  *code_out = 0 when no kernel recorded a fault. */
+H3B_API int h3b_device_error(int* code_out, int clear);
+
+/* ------------------------------------------------------------------ quantize
+ * amax_out[0] = max |x| over a [rows, cols] bf16 matrix with row stride ldx
+ * (elements).  Replaces the global-amax half of the maiku quantizer behind
+ * h3_inference/nvfp4.py:20-23 (the three-level recipe's fp32 global scale).
+ * amax_out is overwritten (zeroed on `stream`, then reduced into).            */
+H3B_API int h3b_amax_bf16(const void* x, int64_t rows, int64_t cols, int64_t ldx, float* amax_out,
+                  void* stream);
+
+/* NVFP4 quantize/pack.  Replaces _quantize / _quantize_padded + _swizzle
+ * (h3_inference/nvfp4.py:20-46):
+ *   x      bf16 [M, K], row stride ldx (elements), K % 64 == 0
+ *   amax   device fp32 scalar (from h3b_amax_bf16 or a fused producer); the
+ *          global scale is gs = amax / 2688 (gs = 1 when amax == 0).  When
+ *          amax is NULL, gs_in is used instead (pass 1.0 for the two-level
+ *          scheme of the reference).
+ *   gs_out device fp32 scalar receiving gs (may be NULL)
+ *   q      u8 [Mpad, K/2]: E2M1 codes, low nibble = even K index
+ *   sf     e4m3 scales, layout H3B_SF_ROWMAJOR [Mpad, K/16] or
+ *          H3B_SF_SWIZZLED (Mpad % 128 == 0)
+ *   Mpad   >= M; rows M..Mpad-1 get zero codes and zero scales.              */
+H3B_API int h3b_nvfp4_quantize(const void* x, int64_t M, int64_t K, int64_t ldx, const float* amax,
+                       float gs_in, float* gs_out, void* q, void* sf, int sf_layout, int64_t Mpad,
+                       void* stream);
+
+/* NVFP4 unpack: out bf16 [M, K] = bf16((LUT[code] * s) * gs).  The CPU decode
+ * this mirrors is h3_inference/render.py:178-183 (plus the global scale).
+ * sf is laid out as sf_layout over `sf_rows` rows (>= M).                    */
+H3B_API int h3b_nvfp4_dequantize(const void* q, const void* sf, int sf_layout, int64_t sf_rows,
+                         const float* gs, int64_t M, int64_t K, void* out, void* stream);
+
+/* ------------------------------------------------------------------ GEMM
+ * D[M, N] (bf16, row stride ldd) = epilogue( alpha * (A * sfA) x (B * sfB)^T )
+ * with alpha = gsA * gsB (device fp32; NULL means 1).  gsB holds one value
+ * per `gsb_seg` output columns (gsb_seg % 128 == 0, N % gsb_seg == 0), or a
+ * single value when gsb_seg == 0 -- this lets weights that were quantized
+ * separately (to_q, to_k, to_v) run as one N-concatenated GEMM.  Replaces
+ * QuantizedActivation.mm / torch._scaled_mm (h3_inference/nvfp4.py:112-115)
+ * and, through the epilogue, the bias/GELU/residual work around it
+ * (h3_inference/kernels/ffn_qkvo_gemms.py:10-54).
+ *   A    u8 [a_rows, K/2] packed E2M1, a_rows % 128 == 0, a_rows >= M
+ *   sfA  swizzled e4m3 scales of A (a_rows rows)
+ *   B    u8 [N, K/2] packed E2M1 (the weight, K-major), N % 128 == 0
+ *   sfB  swizzled e4m3 scales of B
+ *   K    % 256 == 0
+ *   epilogue, in order: v = acc*alpha; v += bias[n] (bf16, optional);
+ *   v = act(v); v += residual[m, n] (bf16, row stride ldr, optional);
+ *   D = bf16(v); amax_out (optional) is atomically max-reduced with |D|
+ *   (the caller zeroes it first).                                            */
+H3B_API int h3b_nvfp4_gemm(const void* A, const void* sfA, const float* gsA, int64_t M, int64_t a_rows,
+                   const void* B, const void* sfB, const float* gsB, int64_t gsb_seg, int64_t N,
+                   int64_t K, const void* bias, const void* residual, int64_t ldr, int act,
+                   void* D, int64_t ldd, float* amax_out, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* H3B_H_ */
