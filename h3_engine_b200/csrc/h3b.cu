@@ -14,6 +14,7 @@
 #include "common.cuh"
 #include "quant.cuh"
 #include "gemm_nvfp4.cuh"
+#include "norm.cuh"
 
 namespace h3b {
 
@@ -244,6 +245,62 @@ int h3b_nvfp4_gemm(const void* A, const void* sfA, const float* gsA, int64_t M, 
   dim3 grid((unsigned)((N + gemm::BN - 1) / gemm::BN), (unsigned)((M + gemm::BM - 1) / gemm::BM));
   gemm::k_gemm_nvfp4<<<grid, gemm::THREADS, gemm::SMEM_BYTES, static_cast<cudaStream_t>(stream)>>>(
       args);
+  return launched(cudaGetLastError());
+}
+
+// ------------------------------------------------------------------ RMSNorm -> NVFP4
+static int norm_args(NormArgs& a, const void* x, int64_t M, int64_t K, int64_t ldx,
+                     const void* gamma, float eps, const void* shift, const void* scale,
+                     const int32_t* mod_idx) {
+  if (M < 0 || K <= 0 || K % 256 || ldx < K || ldx % 8) return H3B_ERR_INVALID_ARG;
+  if (!gamma || (M > 0 && !x) || ((shift == nullptr) != (scale == nullptr))) return H3B_ERR_INVALID_ARG;
+  if ((M > 0 && !aligned16(x)) || !aligned16(gamma) || (shift && !aligned16(shift)) ||
+      (scale && !aligned16(scale)))
+    return H3B_ERR_ALIGNMENT;
+  a.x = static_cast<const __nv_bfloat16*>(x);
+  a.gamma = static_cast<const __nv_bfloat16*>(gamma);
+  a.shift = static_cast<const __nv_bfloat16*>(shift);
+  a.scale = static_cast<const __nv_bfloat16*>(scale);
+  a.mod_idx = mod_idx;
+  a.ldx = ldx;
+  a.M = M;
+  a.K = K;
+  a.eps = eps;
+  return H3B_OK;
+}
+
+int h3b_rmsnorm_stats(const void* x, int64_t M, int64_t K, int64_t ldx, const void* gamma,
+                      float eps, const void* shift, const void* scale, const int32_t* mod_idx,
+                      float* rstd_out, float* amax_out, void* stream) {
+  NormArgs a;
+  int rc = norm_args(a, x, M, K, ldx, gamma, eps, shift, scale, mod_idx);
+  if (rc != H3B_OK) return rc;
+  if (!amax_out || (M > 0 && !rstd_out)) return H3B_ERR_INVALID_ARG;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (cudaMemsetAsync(amax_out, 0, sizeof(float), st) != cudaSuccess) return H3B_ERR_CUDA;
+  if (M == 0) return H3B_OK;
+  const unsigned blocks = (unsigned)((M + kNormWarps - 1) / kNormWarps);
+  if (K <= kNormCacheChunks * 256)
+    k_rmsnorm_stats<kNormCacheChunks><<<blocks, kNormWarps * 32, 0, st>>>(a, rstd_out, amax_out);
+  else
+    k_rmsnorm_stats<0><<<blocks, kNormWarps * 32, 0, st>>>(a, rstd_out, amax_out);
+  return launched(cudaGetLastError());
+}
+
+int h3b_rmsnorm_quantize(const void* x, int64_t M, int64_t K, int64_t ldx, const void* gamma,
+                         const void* shift, const void* scale, const int32_t* mod_idx,
+                         const float* rstd, const float* amax, float* gs_out, void* q, void* sf,
+                         int64_t Mpad, void* y_out, void* stream) {
+  NormArgs a;
+  int rc = norm_args(a, x, M, K, ldx, gamma, 0.f, shift, scale, mod_idx);
+  if (rc != H3B_OK) return rc;
+  if (!amax || !q || !sf || (M > 0 && !rstd) || Mpad < M || Mpad % 128) return H3B_ERR_INVALID_ARG;
+  if ((reinterpret_cast<uintptr_t>(q) & 3u) || (y_out && !aligned16(y_out))) return H3B_ERR_ALIGNMENT;
+  if (Mpad == 0) return H3B_OK;
+  const unsigned blocks = (unsigned)((Mpad + kNormWarps - 1) / kNormWarps);
+  k_rmsnorm_quant<<<blocks, kNormWarps * 32, 0, static_cast<cudaStream_t>(stream)>>>(
+      a, rstd, amax, gs_out, static_cast<uint8_t*>(q), static_cast<uint8_t*>(sf), Mpad,
+      static_cast<__nv_bfloat16*>(y_out));
   return launched(cudaGetLastError());
 }
 

@@ -143,3 +143,45 @@ def gemm(qa: torch.Tensor, sfa: torch.Tensor, gsa: torch.Tensor | None, M: int,
                                    _p(out), out.stride(0), _p(amax_out), _stream(dev))
     _lib.check(st, "h3b_nvfp4_gemm")
     return out
+
+
+def rmsnorm_quantize(x: torch.Tensor, gamma: torch.Tensor, eps: float, *,
+                     shift: torch.Tensor | None = None, scale: torch.Tensor | None = None,
+                     mod_idx: torch.Tensor | None = None, mpad: int | None = None,
+                     return_y: bool = False, ws: dict | None = None):
+    """Fused RMSNorm(+modulation) -> NVFP4.  Returns (q, sf_swizzled, gs[, y]).
+
+    ``ws`` optionally carries preallocated buffers (keys rstd, amax, q, sf, gs, y).
+    """
+    dev = _need_cuda(x, gamma, shift, scale, mod_idx)
+    x2 = x.reshape(-1, x.shape[-1]) if x.dim() != 2 else x
+    if x2.stride(-1) != 1:
+        x2 = x2.contiguous()
+    M, K = x2.shape
+    Mp = pad_m(M if mpad is None else mpad)
+    ws = {} if ws is None else ws
+
+    def buf(name, n, dtype):
+        t = ws.get(name)
+        if t is None or t.numel() < n or t.dtype != dtype:
+            t = torch.empty(n, dtype=dtype, device=dev)
+            ws[name] = t
+        return t[:n]
+
+    rstd = buf("rstd", max(M, 1), torch.float32)
+    am = buf("amax", 1, torch.float32)
+    q = buf("q", Mp * (K // 2), torch.uint8).view(Mp, K // 2)
+    sf = buf("sf", Mp * (K // 16), torch.uint8)
+    gs = buf("gs", 1, torch.float32)
+    y = buf("y", M * K, torch.bfloat16).view(M, K) if return_y else None
+    if mod_idx is not None and mod_idx.dtype != torch.int32:
+        mod_idx = mod_idx.to(torch.int32)
+    lib = _lib.lib()
+    s = _stream(dev)
+    _lib.check(lib.h3b_rmsnorm_stats(_p(x2), M, K, x2.stride(0), _p(gamma), float(eps), _p(shift),
+                                     _p(scale), _p(mod_idx), _p(rstd), _p(am), s),
+               "h3b_rmsnorm_stats")
+    _lib.check(lib.h3b_rmsnorm_quantize(_p(x2), M, K, x2.stride(0), _p(gamma), _p(shift), _p(scale),
+                                        _p(mod_idx), _p(rstd), _p(am), _p(gs), _p(q), _p(sf), Mp,
+                                        _p(y), s), "h3b_rmsnorm_quantize")
+    return (q, sf, gs, y) if return_y else (q, sf, gs)

@@ -107,6 +107,28 @@ H3B_API int h3b_nvfp4_gemm(const void* A, const void* sfA, const float* gsA, int
                    int64_t K, const void* bias, const void* residual, int64_t ldr, int act,
                    void* D, int64_t ldd, float* amax_out, void* stream);
 
+/* ------------------------------------------------------------------ RMSNorm -> NVFP4
+ * The norm that feeds the QKV and FFN-up GEMMs, fused with the activation
+ * quantization.  Replaces rms_norm / norm_modulate / ada_modulate
+ * (h3_inference/kernels/elementwise_norm_rope.py:19-23,42-52,69-102) and the
+ * QuantizedActivation quantization of their output (h3_inference/nvfp4.py:92-110):
+ *   y[m, k] = bf16( x*rstd*gamma[k] * (1 + scale[idx[m], k]) + shift[idx[m], k] )
+ *   rstd[m] = 1 / sqrt(mean_k x[m,k]^2 + eps)
+ * (modulation optional: shift/scale NULL; idx NULL means table row 0).
+ * K % 256 == 0.  Pass 1 writes rstd [M] and amax_out = max|y| (zeroed on
+ * `stream` first); pass 2 recomputes y and writes E2M1 codes [Mpad, K/2] and
+ * swizzled scales with gs = amax / 2688 (Mpad % 128 == 0), plus y itself
+ * when y_out is non-NULL.                                                   */
+H3B_API int h3b_rmsnorm_stats(const void* x, int64_t M, int64_t K, int64_t ldx, const void* gamma,
+                              float eps, const void* shift, const void* scale,
+                              const int32_t* mod_idx, float* rstd_out, float* amax_out,
+                              void* stream);
+H3B_API int h3b_rmsnorm_quantize(const void* x, int64_t M, int64_t K, int64_t ldx,
+                                 const void* gamma, const void* shift, const void* scale,
+                                 const int32_t* mod_idx, const float* rstd, const float* amax,
+                                 float* gs_out, void* q, void* sf, int64_t Mpad, void* y_out,
+                                 void* stream);
+
 #ifdef __cplusplus
 }
 #endif

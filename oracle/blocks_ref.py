@@ -1,0 +1,62 @@
+"""CPU oracle for the DiT sub-blocks -- TEST INFRASTRUCTURE ONLY (see
+``oracle/nvfp4_ref.py`` for who may import it).
+
+Restates, in numpy:
+* RMSNorm as torch computes it for bf16 input (fp32 math, one bf16 rounding
+  of ``x * rstd * gamma``): ``h3_inference/kernels/elementwise_norm_rope.py:19-23``;
+  pinned against the reference's nn.RMSNorm by ``tests/golden/blocks_golden.npz``.
+* adaLN modulation ``norm(x) * (1 + scale[idx]) + shift[idx]``:
+  ``h3_inference/kernels/elementwise_norm_rope.py:42-52``.
+* The FFN sub-block of the GELU/bias configuration: RMSNorm -> NVFP4 linear
+  (+b1) -> GELU-tanh -> NVFP4 re-quantization -> NVFP4 linear (+b2) ->
+  residual add (the row shim ``ffn`` at ``h3_inference/kernels/ffn_qkvo_gemms.py:45-54``
+  plus ``gate_residual`` at ``h3_inference/kernels/elementwise_norm_rope.py:150-163``
+  with gate 1).
+Every NVFP4 step uses ``nvfp4_ref.quantize`` (bit-exact recipe) and
+fp64-accumulated GEMMs rounded once to bf16.
+"""
+from __future__ import annotations
+
+import numpy as np
+
+from . import nvfp4_ref as R
+
+
+def rmsnorm(x, gamma, eps: float, shift=None, scale=None, mod_idx=None) -> np.ndarray:
+    """bf16 RMSNorm (+ optional modulation), returned as bf16 values in fp32."""
+    x = R.bf16_round(x).astype(np.float64)
+    g = R.bf16_round(gamma).astype(np.float64)
+    ms = np.mean(x * x, axis=-1, keepdims=True)
+    y = x / np.sqrt(ms + eps) * g
+    if scale is not None:
+        idx = np.zeros(x.shape[0], dtype=np.int64) if mod_idx is None else np.asarray(mod_idx)
+        sc = R.bf16_round(scale).astype(np.float64)[idx]
+        sh = R.bf16_round(shift).astype(np.float64)[idx]
+        y = y * (1.0 + sc) + sh
+    return R.bf16_round(y.astype(np.float32))
+
+
+def nvfp4_linear_from_bf16(a_bf16, qw, sw, gw, bias=None, act=None, residual=None, gs_a=None):
+    """Quantize bf16 activations with the recipe (optionally with a given gs),
+    GEMM against a quantized weight, epilogue, bf16 out."""
+    M = a_bf16.shape[0]
+    qa, sa, ga = R.quantize(a_bf16, gs=gs_a)
+    y = R.gemm_ref(qa, sa, ga, qw, sw, gw, M, qw.shape[0])
+    if bias is not None:
+        y = y + R.bf16_round(bias).astype(np.float64)[None, :]
+    if act == "gelu_tanh":
+        y = R.gelu_tanh(y)
+    if residual is not None:
+        y = y + R.bf16_round(residual).astype(np.float64)
+    return R.bf16_round(y.astype(np.float32)), ga
+
+
+def ffn_block(x, gamma, eps, w1q, b1, w2q, b2, gs_u=None):
+    """FFN sub-block.  ``w1q``/``w2q`` are (q, sf_rowmajor, gs) triples of the
+    quantized weights.  ``gs_u`` optionally forces the re-quantization global
+    scale (used when checking a row sample of a tensor too large for the
+    oracle, with the global scale taken from the full GPU run)."""
+    h = rmsnorm(x, gamma, eps)
+    u, _ = nvfp4_linear_from_bf16(h, *w1q, bias=b1, act="gelu_tanh")
+    y, gu = nvfp4_linear_from_bf16(u, *w2q, bias=b2, residual=x, gs_a=gs_u)
+    return y, h, u
