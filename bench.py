@@ -193,9 +193,10 @@ def run_ours(args) -> None:
 
     w1, b1, w2, b2, gamma = make_weights(dev)
     blk = FFNBlock(w1, b1, w2, b2, gamma, EPS)
-    x = make_tokens(rank, dev)
+    tokens = args.tokens
+    x = make_tokens(rank, dev, tokens)
     y = torch.empty_like(x)
-    flops = gemm_flops(TOKENS)
+    flops = gemm_flops(tokens)
 
     for _ in range(args.warmup):
         blk(x, out=y)
@@ -268,7 +269,7 @@ def run_ours(args) -> None:
             "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "nvfp4 (e2m1 x e4m3/16 x fp32), fp32 accumulate, bf16 out",
             "data": "synthetic (seeded, shapes/distributions of the FFN sub-block config)",
-            "config": {"workload": WORKLOAD, "tokens_per_gpu": TOKENS, "hidden": HIDDEN,
+            "config": {"workload": WORKLOAD, "tokens_per_gpu": tokens, "hidden": HIDDEN,
                        "ffn": FFN, "parallelism": f"token-sharded x{world}, weights replicated",
                        "l2": "working set ~1.3 GB per step > 126 MB L2 (no flush needed)"},
             "e2e": {"value": world * flops / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s",
@@ -328,7 +329,9 @@ def main() -> None:
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["h3b", "reference"], default="h3b")
-    ap.add_argument("--cpu-tokens", type=int, default=512,
+    ap.add_argument("--tokens", type=int, default=TOKENS,
+                    help="tokens per GPU (default: the configured 32768; smaller for ncu captures)")
+    ap.add_argument("--cpu-tokens", type=int, default=1024,
                     help="token sample for the CPU baseline")
     ap.add_argument("--no-extras", action="store_true",
                     help="skip the library GEMM comparison and the CPU baseline (profiling runs)")
