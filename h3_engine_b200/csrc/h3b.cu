@@ -304,4 +304,79 @@ int h3b_rmsnorm_quantize(const void* x, int64_t M, int64_t K, int64_t ldx, const
   return launched(cudaGetLastError());
 }
 
+// ------------------------------------------------------------------ RMSNorm -> NVFP4, no allocation
+// Some callers of this library cannot allocate device memory while they run:
+// inference servers that hand every kernel a fixed, pre-planned memory pool,
+// plugin hosts whose execute callback must not touch the allocator, and code
+// that runs while another allocator owns the device.  Such callers cannot
+// provide the per-row rstd / amax scratch that h3b_rmsnorm_stats and
+// h3b_rmsnorm_quantize pass between them.  h3b_rmsnorm_quantize_noalloc runs
+// the same two kernels with that scratch in a fixed array compiled into the
+// library: every GPU that loads libh3b.so holds it (kNoAllocRows * 4 + 256
+// bytes) until the process exits.  All calls on a device share the array, so
+// calls that overlap on the GPU (different streams, no ordering between
+// them) race; calls on one stream, or otherwise ordered, are safe.
+constexpr int64_t kNoAllocRows = 131072;
+static __device__ __align__(256) float g_noalloc_scratch[kNoAllocRows + 64];
+
+namespace h3b {
+constexpr int kNoAllocMaxDevices = 64;
+static float* g_noalloc_ptr[kNoAllocMaxDevices];
+static std::mutex g_noalloc_mu;
+
+// Device address of g_noalloc_scratch on the current device.  In host code the
+// symbol itself is only a host-side stand-in, so the address is looked up with
+// cudaGetSymbolAddress once per device (with that device current) and cached.
+static int noalloc_scratch(float** out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return H3B_ERR_CUDA;
+  if (dev < 0 || dev >= kNoAllocMaxDevices) return H3B_ERR_UNSUPPORTED;
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (g_noalloc_ptr[dev] == nullptr) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess || p == nullptr)
+      return H3B_ERR_CUDA;
+    g_noalloc_ptr[dev] = static_cast<float*>(p);
+  }
+  *out = g_noalloc_ptr[dev];
+  return H3B_OK;
+}
+}  // namespace h3b
+
+int h3b_rmsnorm_quantize_noalloc(const void* x, int64_t M, int64_t K, int64_t ldx,
+                                 const void* gamma, float eps, const void* shift,
+                                 const void* scale, const int32_t* mod_idx, float* gs_out,
+                                 void* q, void* sf, int64_t Mpad, void* stream) {
+  if (M > kNoAllocRows) return H3B_ERR_INVALID_ARG;   // beyond the fixed scratch
+  NormArgs a;
+  int rc = norm_args(a, x, M, K, ldx, gamma, eps, shift, scale, mod_idx);
+  if (rc != H3B_OK) return rc;
+  if (!q || !sf || Mpad < M || Mpad % 128) return H3B_ERR_INVALID_ARG;
+  if (reinterpret_cast<uintptr_t>(q) & 3u) return H3B_ERR_ALIGNMENT;
+  if (Mpad == 0) return H3B_OK;
+  rc = check_sm100();
+  if (rc != H3B_OK) return rc;
+  float* scratch = nullptr;
+  rc = noalloc_scratch(&scratch);
+  if (rc != H3B_OK) return rc;
+  float* rstd = scratch;                    // [kNoAllocRows]
+  float* amax = scratch + kNoAllocRows;     // 1 float, 256-byte aligned
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  // the array keeps the previous call's contents: amax must start at zero
+  if (cudaMemsetAsync(amax, 0, sizeof(float), st) != cudaSuccess) return H3B_ERR_CUDA;
+  const unsigned stat_blocks = (unsigned)((M + kNormWarps - 1) / kNormWarps);
+  if (M > 0) {
+    if (K <= kNormCacheChunks * 256)
+      k_rmsnorm_stats<kNormCacheChunks><<<stat_blocks, kNormWarps * 32, 0, st>>>(a, rstd, amax);
+    else
+      k_rmsnorm_stats<0><<<stat_blocks, kNormWarps * 32, 0, st>>>(a, rstd, amax);
+    rc = launched(cudaGetLastError());
+    if (rc != H3B_OK) return rc;
+  }
+  const unsigned q_blocks = (unsigned)((Mpad + kNormWarps - 1) / kNormWarps);
+  k_rmsnorm_quant<<<q_blocks, kNormWarps * 32, 0, st>>>(
+      a, rstd, amax, gs_out, static_cast<uint8_t*>(q), static_cast<uint8_t*>(sf), Mpad, nullptr);
+  return launched(cudaGetLastError());
+}
+
 }  // extern "C"

@@ -129,6 +129,28 @@ H3B_API int h3b_rmsnorm_quantize(const void* x, int64_t M, int64_t K, int64_t ld
                                  float* gs_out, void* q, void* sf, int64_t Mpad, void* y_out,
                                  void* stream);
 
+/* ------------------------------------------------------------------ no-allocation variant
+ * No counterpart in the reference.  The same RMSNorm(+modulation) -> NVFP4
+ * result as h3b_rmsnorm_stats followed by h3b_rmsnorm_quantize (y_out not
+ * available), for callers that cannot allocate device memory while they run
+ * -- servers that give kernels a fixed pre-planned memory pool, plugin hosts
+ * whose execute path must not call the allocator -- and so cannot provide the
+ * rstd / amax scratch the two-call form needs.  The scratch is a fixed array
+ * inside libh3b.so (every GPU that loads the library keeps it, about 512 KiB,
+ * until the process exits); the call itself allocates nothing.
+ *   M <= 131072 rows, else H3B_ERR_INVALID_ARG; other limits as above.
+ *   The first call on a device looks up the array's device address (once per
+ *   device, with that device current); make that first call before any stream
+ *   capture.
+ *   All calls on a device share the array: calls that overlap on the GPU
+ *   race.  Order them (one stream, or events) if more than one can be in
+ *   flight.                                                                  */
+H3B_API int h3b_rmsnorm_quantize_noalloc(const void* x, int64_t M, int64_t K, int64_t ldx,
+                                         const void* gamma, float eps, const void* shift,
+                                         const void* scale, const int32_t* mod_idx,
+                                         float* gs_out, void* q, void* sf, int64_t Mpad,
+                                         void* stream);
+
 #ifdef __cplusplus
 }
 #endif
