@@ -21,7 +21,7 @@
 #include "common.cuh"
 
 namespace h3b {
-namespace gemm {
+namespace gemm_v1 {
 
 constexpr int BM = 128;
 constexpr int BN = 256;
@@ -279,5 +279,320 @@ __global__ void __launch_bounds__(THREADS, 1) k_gemm_nvfp4(const __grid_constant
   }
 }
 
+}  // namespace gemm_v1
+
+// ============================================================================
+// Persistent variant (the production kernel).
+//
+// grid = min(#tiles, #SMs); CTA b processes tiles b, b+grid, ... in M-major
+// raster (consecutive tiles share the A row-block, so concurrently running
+// CTAs reuse it from L2).  The producer and the MMA issuer run ahead across
+// tile boundaries, so the operand pipeline never drains between tiles.
+//   warp 0     TMA producer (3-stage ring, 54 KiB per stage)
+//   warp 1     TMEM allocator + single-thread MMA issuer
+//   warps 2-9  epilogue, two warps per TMEM lane quadrant (128 columns each):
+//              they pull the whole 128x256 fp32 accumulator into registers,
+//              hand TMEM back to the MMA warp (acc_empty, 8 arrivals), then
+//              apply alpha / bias / GELU / residual, convert to bf16, stage
+//              64-column chunks in a 128B-swizzled 4 KiB buffer per warp and
+//              write them with TMA stores (which clip rows >= M), while the
+//              next tile's mainloop runs.
+// Every wait is bounded; there is no barrier among the epilogue warps, so a
+// timeout in one role always unwinds the whole CTA.
+// ============================================================================
+namespace gemm {
+
+constexpr int BM = 128;
+constexpr int BN = 256;
+constexpr int KB_ELEMS = 256;
+constexpr int KB_BYTES = KB_ELEMS / 2;
+constexpr int STAGES = 3;
+constexpr int A_BYTES = BM * KB_BYTES;
+constexpr int B_BYTES = BN * KB_BYTES;
+constexpr int SF_ATOM = 512;
+constexpr int SFA_BYTES = (BM / 128) * 4 * SF_ATOM;
+constexpr int SFB_BYTES = (BN / 128) * 4 * SF_ATOM;
+constexpr int STAGE_BYTES = A_BYTES + B_BYTES + SFA_BYTES + SFB_BYTES;
+constexpr int EPI_WARPS = 8;
+constexpr int OUT_CHUNK_COLS = 64;                       // bf16 columns per TMA store
+constexpr int OUT_WARP_BYTES = 32 * OUT_CHUNK_COLS * 2;  // 4 KiB, one 128B-swizzled box
+constexpr int OUT_OFFSET = STAGES * STAGE_BYTES;
+constexpr int BAR_OFFSET = OUT_OFFSET + EPI_WARPS * OUT_WARP_BYTES;
+constexpr int SMEM_BYTES = BAR_OFFSET + 256 + 1024;
+constexpr int THREADS = 64 + EPI_WARPS * 32;
+constexpr uint32_t TMEM_COLS = 512;
+constexpr uint32_t ACC_COL = 0;
+constexpr uint32_t SF_COL = 256;
+constexpr uint32_t SF_STAGE_COLS = 4 * 4 + 4 * 8;
+constexpr uint32_t IDESC = (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) |
+                           ((uint32_t)(BM >> 4) << 24);
+
+static_assert(STAGE_BYTES % 1024 == 0 && OUT_OFFSET % 1024 == 0, "swizzle alignment");
+static_assert(SF_COL + STAGES * SF_STAGE_COLS <= TMEM_COLS, "TMEM budget");
+static_assert(SMEM_BYTES <= 232448, "shared memory budget");
+
+struct Args {
+  CUtensorMap tmap_a;      // u8 [a_rows, K/2],  box 128 B x 128 rows, 128B swizzle
+  CUtensorMap tmap_b;      // u8 [N, K/2],       box 128 B x 256 rows, 128B swizzle
+  CUtensorMap tmap_d;      // bf16 [M, N] (pitch ldd), box 64 x 32, 128B swizzle
+  const uint8_t* sfa;
+  const uint8_t* sfb;
+  const float* gs_a;
+  const float* gs_b;
+  const __nv_bfloat16* bias;
+  const __nv_bfloat16* residual;
+  float* amax_out;
+  long long ldr;
+  int M, N, K;
+  int sf_atoms_k;
+  int act;
+  int gsb_seg;
+  int n_tiles;
+  int num_tiles;
+};
+
+__device__ __forceinline__ float gelu_tanh(float v) { return gemm_v1::gelu_tanh(v); }
+
+__global__ void __launch_bounds__(THREADS, 1) k_gemm_nvfp4(const __grid_constant__ Args p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + BAR_OFFSET);
+  uint64_t* full = bars;
+  uint64_t* empty = bars + STAGES;
+  uint64_t* acc_full = bars + 2 * STAGES;
+  uint64_t* acc_empty = bars + 2 * STAGES + 1;
+  uint64_t* drain = bars + 2 * STAGES + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 3);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int num_kb = p.K / KB_ELEMS;
+
+  auto sA = [&](int s) { return smem + s * STAGE_BYTES; };
+  auto sB = [&](int s) { return smem + s * STAGE_BYTES + A_BYTES; };
+  auto sSFA = [&](int s) { return smem + s * STAGE_BYTES + A_BYTES + B_BYTES; };
+  auto sSFB = [&](int s) { return smem + s * STAGE_BYTES + A_BYTES + B_BYTES + SFA_BYTES; };
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(smem_u32(&full[s]), 1);
+      mbar_init(smem_u32(&empty[s]), 1);
+    }
+    mbar_init(smem_u32(acc_full), 1);
+    mbar_init(smem_u32(acc_empty), EPI_WARPS);
+    mbar_init(smem_u32(drain), 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(tmem_slot), TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      prefetch_tmap(&p.tmap_a);
+      prefetch_tmap(&p.tmap_b);
+      uint32_t g = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x) {
+        const int m0 = (t / p.n_tiles) * BM, n0 = (t % p.n_tiles) * BN;
+        const bool b_hi = (n0 + 128) < p.N;
+        const uint32_t tx = A_BYTES + B_BYTES + SFA_BYTES + (b_hi ? 2 : 1) * 4 * SF_ATOM;
+        const uint8_t* sfa_row = p.sfa + (size_t)(m0 / 128) * p.sf_atoms_k * SF_ATOM;
+        const uint8_t* sfb_row0 = p.sfb + (size_t)(n0 / 128) * p.sf_atoms_k * SF_ATOM;
+        const uint8_t* sfb_row1 = sfb_row0 + (size_t)p.sf_atoms_k * SF_ATOM;
+        for (int kb = 0; kb < num_kb; ++kb, ++g) {
+          const int s = g % STAGES;
+          const uint32_t ph = (g / STAGES) & 1;
+          if (g >= STAGES && !mbar_wait(smem_u32(&empty[s]), ph ^ 1, abort_flag)) {
+            record_error(H3B_ERR_TIMEOUT);
+            *abort_flag = 1;
+            ok = false;
+            break;
+          }
+          const uint32_t fb = smem_u32(&full[s]);
+          mbar_expect_tx(fb, tx);
+          tma_load_2d(smem_u32(sA(s)), &p.tmap_a, kb * KB_BYTES, m0, fb);
+          tma_load_2d(smem_u32(sB(s)), &p.tmap_b, kb * KB_BYTES, n0, fb);
+          bulk_load(smem_u32(sSFA(s)), sfa_row + (size_t)kb * 4 * SF_ATOM, 4 * SF_ATOM, fb);
+          bulk_load(smem_u32(sSFB(s)), sfb_row0 + (size_t)kb * 4 * SF_ATOM, 4 * SF_ATOM, fb);
+          if (b_hi)
+            bulk_load(smem_u32(sSFB(s)) + 4 * SF_ATOM, sfb_row1 + (size_t)kb * 4 * SF_ATOM,
+                      4 * SF_ATOM, fb);
+        }
+      }
+      if (!ok || *abort_flag) {
+        // Let every copy already in flight land before the CTA can exit.
+        for (uint32_t q = g > (uint32_t)STAGES ? g - STAGES : 0; q < g; ++q)
+          mbar_wait(smem_u32(&full[q % STAGES]), (q / STAGES) & 1, nullptr);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      uint32_t g = 0, i = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x, ++i) {
+        if (i > 0 && !mbar_wait(smem_u32(acc_empty), (i - 1) & 1, abort_flag)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        for (int kb = 0; kb < num_kb; ++kb, ++g) {
+          const int s = g % STAGES;
+          const uint32_t ph = (g / STAGES) & 1;
+          if (!mbar_wait(smem_u32(&full[s]), ph, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          // Scale atoms of this k-block -> tensor memory (one 32x128b.warpx4
+          // copy per 128 rows per MMA k-step), then the four MMAs that read them.
+          const uint32_t sf_t = tmem + SF_COL + s * SF_STAGE_COLS;
+          const uint32_t sfa_s = smem_u32(sSFA(s));
+          const uint32_t sfb_s = smem_u32(sSFB(s));
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk) {
+            tc_cp_32x128b_warpx4(sf_t + kk * 4, desc_sf_atom(sfa_s + kk * SF_ATOM));
+            tc_cp_32x128b_warpx4(sf_t + 16 + kk * 8, desc_sf_atom(sfb_s + kk * SF_ATOM));
+            tc_cp_32x128b_warpx4(sf_t + 16 + kk * 8 + 4,
+                                 desc_sf_atom(sfb_s + 4 * SF_ATOM + kk * SF_ATOM));
+          }
+          const uint32_t a_s = smem_u32(sA(s)), b_s = smem_u32(sB(s));
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk) {
+            tc_mma_nvf4(tmem + ACC_COL, desc_kmajor_sw128(a_s + kk * 32),
+                        desc_kmajor_sw128(b_s + kk * 32), IDESC, sf_t + kk * 4,
+                        sf_t + 16 + kk * 8, (kb | kk) != 0);
+          }
+          tc_commit(smem_u32(&empty[s]));
+        }
+        if (!ok) break;
+        tc_commit(smem_u32(acc_full));
+      }
+      if (!ok) {
+        if (!*abort_flag) {
+          record_error(H3B_ERR_TIMEOUT);
+          *abort_flag = 1;
+        }
+        tc_commit(smem_u32(drain));
+        mbar_wait(smem_u32(drain), 0, nullptr);
+      }
+    }
+  } else {
+    const int ew = warp - 2;
+    const int qd = warp & 3;          // TMEM lane quadrant this warp may access
+    const int half = ew >> 2;         // which 128 of the 256 accumulator columns
+    uint8_t* stage = smem + OUT_OFFSET + ew * OUT_WARP_BYTES;
+    const uint32_t stage_s = smem_u32(stage);
+    const float gsa = p.gs_a ? __ldg(p.gs_a) : 1.f;
+    float amax = 0.f;
+    uint32_t i = 0;
+    if (lane == 0) prefetch_tmap(&p.tmap_d);
+    for (int t = blockIdx.x; t < p.num_tiles; t += gridDim.x, ++i) {
+      const int m0 = (t / p.n_tiles) * BM, n0 = (t % p.n_tiles) * BN;
+      const bool ready = __all_sync(0xffffffffu, mbar_wait(smem_u32(acc_full), i & 1, abort_flag));
+      if (!ready) {
+        if (!*abort_flag) {
+          record_error(H3B_ERR_TIMEOUT);
+          *abort_flag = 1;
+        }
+        break;
+      }
+      tc_fence_after();
+      uint32_t acc[128];
+      const uint32_t taddr = tmem + ACC_COL + ((uint32_t)(qd * 32) << 16) + half * 128;
+      tmem_ld_32x32b_x64(taddr, acc);
+      tmem_ld_32x32b_x64(taddr + 64, acc + 64);
+      tmem_ld_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_u32(acc_empty));
+
+      const int n_base = n0 + half * 128;
+      if (n_base < p.N && m0 + qd * 32 < p.M) {   // warp-uniform: this warp's box has rows
+        const int row = m0 + qd * 32 + lane;
+        const bool row_ok = row < p.M;
+        const float alpha =
+            gsa * (p.gs_b ? __ldg(p.gs_b + (p.gsb_seg ? n_base / p.gsb_seg : 0)) : 1.f);
+#pragma unroll
+        for (int c = 0; c < 2; ++c) {
+          if (lane == 0) bulk_wait_read0();   // staging buffer free again
+          __syncwarp();
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            const int col = n_base + c * 64 + j * 8;
+            float v[8];
+#pragma unroll
+            for (int e = 0; e < 8; ++e) v[e] = __uint_as_float(acc[c * 64 + j * 8 + e]) * alpha;
+            if (p.bias) {
+              const uint4 b = __ldg(reinterpret_cast<const uint4*>(p.bias + col));
+              const uint32_t bw[4] = {b.x, b.y, b.z, b.w};
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                v[2 * e] += __uint_as_float(bw[e] << 16);
+                v[2 * e + 1] += __uint_as_float(bw[e] & 0xFFFF0000u);
+              }
+            }
+            if (p.act == H3B_ACT_GELU_TANH) {
+#pragma unroll
+              for (int e = 0; e < 8; ++e) v[e] = gelu_tanh(v[e]);
+            }
+            if (p.residual && row_ok) {
+              const uint4 b =
+                  __ldg(reinterpret_cast<const uint4*>(p.residual + (size_t)row * p.ldr + col));
+              const uint32_t bw[4] = {b.x, b.y, b.z, b.w};
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                v[2 * e] += __uint_as_float(bw[e] << 16);
+                v[2 * e + 1] += __uint_as_float(bw[e] & 0xFFFF0000u);
+              }
+            }
+            uint32_t o[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              o[e] = pack_bf16x2(v[2 * e], v[2 * e + 1]);
+              if (row_ok) {
+                amax = fmaxf(amax, fabsf(__uint_as_float(o[e] << 16)));
+                amax = fmaxf(amax, fabsf(__uint_as_float(o[e] & 0xFFFF0000u)));
+              }
+            }
+            // 128B swizzle: 16-byte chunk j of row `lane` sits at chunk j ^ (lane % 8)
+            *reinterpret_cast<uint4*>(stage + lane * 128 + ((j ^ (lane & 7)) << 4)) =
+                make_uint4(o[0], o[1], o[2], o[3]);
+          }
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            tma_store_2d(&p.tmap_d, stage_s, n_base + c * OUT_CHUNK_COLS, m0 + qd * 32);
+            bulk_commit();
+          }
+        }
+      }
+    }
+    if (lane == 0) bulk_wait0();
+    if (p.amax_out) {
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+      if (lane == 0 && amax > 0.f)
+        atomicMax(reinterpret_cast<unsigned int*>(p.amax_out), __float_as_uint(amax));
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem, TMEM_COLS);
+  }
+}
+
 }  // namespace gemm
+
 }  // namespace h3b

@@ -7,7 +7,10 @@
 #include <cudaTypedefs.h>
 #include <cuda_fp16.h>
 
+#include <algorithm>
 #include <atomic>
+#include <cstdlib>
+#include <cstring>
 #include <cstdio>
 #include <mutex>
 
@@ -79,9 +82,71 @@ static int make_tmap_u8_sw128(CUtensorMap* map, const void* base, uint64_t rows,
   return r == CUDA_SUCCESS ? H3B_OK : H3B_ERR_INVALID_ARG;
 }
 
+// 2-D bf16 tensor [rows, cols] (row pitch = pitch_elems), box box_cols x box_rows,
+// 128-byte swizzle (box_cols * 2 must be 128).
+static int make_tmap_bf16_sw128(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols,
+                                uint64_t pitch_elems, uint32_t box_cols, uint32_t box_rows) {
+  auto fn = encode_fn();
+  if (!fn) return H3B_ERR_UNSUPPORTED;
+  cuuint64_t dims[2] = {cols, rows};
+  cuuint64_t strides[1] = {pitch_elems * 2};
+  cuuint32_t box[2] = {box_cols, box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides,
+                  box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? H3B_OK : H3B_ERR_INVALID_ARG;
+}
+
 }  // namespace h3b
 
 using namespace h3b;
+
+// The first (non-persistent, one tile per CTA) GEMM kernel, kept selectable
+// with H3B_GEMM_V1=1 for A/B timing against the persistent kernel.
+static int gemm_v1_launch(const void* A, const void* sfA, const float* gsA, int64_t M,
+                          int64_t a_rows, const void* B, const void* sfB, const float* gsB,
+                          int64_t gsb_seg, int64_t N, int64_t K, const void* bias,
+                          const void* residual, int64_t ldr, int act, void* D, int64_t ldd,
+                          float* amax_out, void* stream) {
+  static std::once_flag attr_once;
+  static cudaError_t attr_err = cudaSuccess;
+  std::call_once(attr_once, [] {
+    attr_err = cudaFuncSetAttribute(gemm_v1::k_gemm_nvfp4,
+                                    cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    gemm_v1::SMEM_BYTES);
+  });
+  if (attr_err != cudaSuccess) return H3B_ERR_CUDA;
+  gemm_v1::Args args;
+  memset(&args, 0, sizeof(args));
+  int rc = make_tmap_u8_sw128(&args.tmap_a, A, (uint64_t)a_rows, (uint64_t)(K / 2),
+                              (uint64_t)(K / 2), gemm_v1::KB_BYTES, gemm_v1::BM);
+  if (rc != H3B_OK) return rc;
+  rc = make_tmap_u8_sw128(&args.tmap_b, B, (uint64_t)N, (uint64_t)(K / 2), (uint64_t)(K / 2),
+                          gemm_v1::KB_BYTES, gemm_v1::BN);
+  if (rc != H3B_OK) return rc;
+  args.sfa = static_cast<const uint8_t*>(sfA);
+  args.sfb = static_cast<const uint8_t*>(sfB);
+  args.gs_a = gsA;
+  args.gs_b = gsB;
+  args.bias = static_cast<const __nv_bfloat16*>(bias);
+  args.residual = static_cast<const __nv_bfloat16*>(residual);
+  args.d = static_cast<__nv_bfloat16*>(D);
+  args.amax_out = amax_out;
+  args.ldr = residual ? ldr : 0;
+  args.ldd = ldd;
+  args.M = (int)M;
+  args.N = (int)N;
+  args.K = (int)K;
+  args.sf_atoms_k = (int)(K / 64);
+  args.act = act;
+  args.gsb_seg = (int)gsb_seg;
+  dim3 grid((unsigned)((N + gemm_v1::BN - 1) / gemm_v1::BN),
+            (unsigned)((M + gemm_v1::BM - 1) / gemm_v1::BM));
+  gemm_v1::k_gemm_nvfp4<<<grid, gemm_v1::THREADS, gemm_v1::SMEM_BYTES,
+                          static_cast<cudaStream_t>(stream)>>>(args);
+  return launched(cudaGetLastError());
+}
 
 extern "C" {
 
@@ -209,6 +274,13 @@ int h3b_nvfp4_gemm(const void* A, const void* sfA, const float* gsA, int64_t M, 
   int st0 = check_sm100();
   if (st0 != H3B_OK) return st0;
 
+  static const bool use_v1 = [] {
+    const char* e = getenv("H3B_GEMM_V1");
+    return e != nullptr && e[0] == '1';
+  }();
+  if (use_v1) return gemm_v1_launch(A, sfA, gsA, M, a_rows, B, sfB, gsB, gsb_seg, N, K, bias,
+                                    residual, ldr, act, D, ldd, amax_out, stream);
+
   static std::once_flag attr_once;
   static cudaError_t attr_err = cudaSuccess;
   std::call_once(attr_once, [] {
@@ -226,23 +298,28 @@ int h3b_nvfp4_gemm(const void* A, const void* sfA, const float* gsA, int64_t M, 
   rc = make_tmap_u8_sw128(&args.tmap_b, B, (uint64_t)N, (uint64_t)(K / 2), (uint64_t)(K / 2),
                           gemm::KB_BYTES, gemm::BN);
   if (rc != H3B_OK) return rc;
+  rc = make_tmap_bf16_sw128(&args.tmap_d, D, (uint64_t)M, (uint64_t)N, (uint64_t)ldd,
+                            gemm::OUT_CHUNK_COLS, 32);
+  if (rc != H3B_OK) return rc;
   args.sfa = static_cast<const uint8_t*>(sfA);
   args.sfb = static_cast<const uint8_t*>(sfB);
   args.gs_a = gsA;
   args.gs_b = gsB;
   args.bias = static_cast<const __nv_bfloat16*>(bias);
   args.residual = static_cast<const __nv_bfloat16*>(residual);
-  args.d = static_cast<__nv_bfloat16*>(D);
   args.amax_out = amax_out;
   args.ldr = residual ? ldr : 0;
-  args.ldd = ldd;
   args.M = (int)M;
   args.N = (int)N;
   args.K = (int)K;
   args.sf_atoms_k = (int)(K / 64);
   args.act = act;
   args.gsb_seg = (int)gsb_seg;
-  dim3 grid((unsigned)((N + gemm::BN - 1) / gemm::BN), (unsigned)((M + gemm::BM - 1) / gemm::BM));
+  args.n_tiles = (int)((N + gemm::BN - 1) / gemm::BN);
+  const int64_t num_tiles = (int64_t)args.n_tiles * ((M + gemm::BM - 1) / gemm::BM);
+  if (num_tiles > INT32_MAX) return H3B_ERR_INVALID_ARG;
+  args.num_tiles = (int)num_tiles;
+  const int grid = (int)std::min<int64_t>(num_tiles, num_sms());
   gemm::k_gemm_nvfp4<<<grid, gemm::THREADS, gemm::SMEM_BYTES, static_cast<cudaStream_t>(stream)>>>(
       args);
   return launched(cudaGetLastError());
