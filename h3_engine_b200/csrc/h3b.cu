@@ -18,6 +18,7 @@
 #include "quant.cuh"
 #include "gemm_nvfp4.cuh"
 #include "norm.cuh"
+#include "rope.cuh"
 
 namespace h3b {
 
@@ -378,6 +379,50 @@ int h3b_rmsnorm_quantize(const void* x, int64_t M, int64_t K, int64_t ldx, const
   k_rmsnorm_quant<<<blocks, kNormWarps * 32, 0, static_cast<cudaStream_t>(stream)>>>(
       a, rstd, amax, gs_out, static_cast<uint8_t*>(q), static_cast<uint8_t*>(sf), Mpad,
       static_cast<__nv_bfloat16*>(y_out));
+  return launched(cudaGetLastError());
+}
+
+// ------------------------------------------------------------------ qk-norm + RoPE
+int h3b_qk_norm_rope(void* qkv, int64_t T, int64_t row_stride, int64_t q_off, int64_t k_off,
+                     int H, int D, const void* wq, const void* wk, float eps, const float* cos,
+                     const float* sin, int R, int64_t cs_stride, void* stream) {
+  if (T < 0 || H <= 0 || (D != 64 && D != 128)) return H3B_ERR_INVALID_ARG;
+  const int epl = D / 32;
+  if (cos != nullptr) {
+    if (!sin || R <= 0 || R > D || R % 2 || (R / 2) % epl || cs_stride < R) return H3B_ERR_INVALID_ARG;
+  } else {
+    R = 0;
+  }
+  if (q_off < 0 || k_off < 0 || row_stride < (int64_t)H * D ||
+      q_off + (int64_t)H * D > row_stride || k_off + (int64_t)H * D > row_stride)
+    return H3B_ERR_INVALID_ARG;
+  if ((row_stride | q_off | k_off) % 8) return H3B_ERR_ALIGNMENT;
+  if (T == 0) return H3B_OK;
+  if (!qkv) return H3B_ERR_INVALID_ARG;
+  if (!aligned16(qkv)) return H3B_ERR_ALIGNMENT;
+  RopeArgs a;
+  a.qkv = static_cast<__nv_bfloat16*>(qkv);
+  a.T = T;
+  a.row_stride = row_stride;
+  a.q_off = q_off;
+  a.k_off = k_off;
+  a.H = H;
+  a.R = R;
+  a.wq = static_cast<const __nv_bfloat16*>(wq);
+  a.wk = static_cast<const __nv_bfloat16*>(wk);
+  a.cos = cos;
+  a.sin = sin;
+  a.cs_stride = cs_stride;
+  a.eps = eps;
+  const int64_t items = T * 2 * H;
+  int64_t blocks = (items + kRopeWarps - 1) / kRopeWarps;
+  const int64_t cap = (int64_t)num_sms() * 16;
+  if (blocks > cap) blocks = cap;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (D == 128)
+    k_qk_norm_rope<128><<<(unsigned)blocks, kRopeWarps * 32, 0, st>>>(a);
+  else
+    k_qk_norm_rope<64><<<(unsigned)blocks, kRopeWarps * 32, 0, st>>>(a);
   return launched(cudaGetLastError());
 }
 

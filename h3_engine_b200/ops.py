@@ -185,3 +185,29 @@ def rmsnorm_quantize(x: torch.Tensor, gamma: torch.Tensor, eps: float, *,
                                         _p(mod_idx), _p(rstd), _p(am), _p(gs), _p(q), _p(sf), Mp,
                                         _p(y), s), "h3b_rmsnorm_quantize")
     return (q, sf, gs, y) if return_y else (q, sf, gs)
+
+
+def qk_norm_rope(qkv: torch.Tensor, heads: int, head_dim: int, *, q_off: int, k_off: int,
+                 wq: torch.Tensor | None, wk: torch.Tensor | None, eps: float,
+                 cos: torch.Tensor | None = None, sin: torch.Tensor | None = None) -> torch.Tensor:
+    """In-place per-head RMSNorm + rotate-half RoPE on the q and k blocks of a
+    packed ``[T, row_stride]`` bf16 activation.  ``cos``/``sin``: fp32 ``[T, R]``."""
+    dev = _need_cuda(qkv, wq, wk, cos, sin)
+    if qkv.dtype != torch.bfloat16 or qkv.stride(-1) != 1:
+        raise ValueError("qkv must be bf16 with a contiguous last dim")
+    q2 = qkv.reshape(-1, qkv.shape[-1]) if qkv.dim() != 2 else qkv
+    T = q2.shape[0]
+    R, cs = 0, 0
+    if cos is not None:
+        if cos.dtype != torch.float32 or sin is None or sin.dtype != torch.float32:
+            raise TypeError("cos/sin must be fp32")
+        cos = cos.reshape(T, -1)
+        sin = sin.reshape(T, -1)
+        if cos.stride(-1) != 1 or sin.stride(-1) != 1 or cos.stride(0) != sin.stride(0):
+            cos, sin = cos.contiguous(), sin.contiguous()
+        R, cs = cos.shape[1], cos.stride(0)
+    st = _lib.lib().h3b_qk_norm_rope(_p(q2), T, q2.stride(0), q_off, k_off, heads, head_dim,
+                                     _p(wq), _p(wk), float(eps), _p(cos), _p(sin), R, cs,
+                                     _stream(dev))
+    _lib.check(st, "h3b_qk_norm_rope")
+    return qkv

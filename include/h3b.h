@@ -129,6 +129,21 @@ H3B_API int h3b_rmsnorm_quantize(const void* x, int64_t M, int64_t K, int64_t ld
                                  float* gs_out, void* q, void* sf, int64_t Mpad, void* y_out,
                                  void* stream);
 
+/* ------------------------------------------------------------------ qk-norm + RoPE
+ * In place on the q and k head blocks of a packed QKV activation
+ * qkv[T, row_stride] (bf16): head h of q starts at column q_off + h*D, of k
+ * at k_off + h*D.  Per head vector: RMSNorm over D with weight wq / wk (NULL:
+ * no norm), then rotate-half RoPE over the first R dims with the (T, R) fp32
+ * cos/sin tables (row stride cs_stride; NULL cos: no RoPE), dims >= R pass
+ * through.  Replaces qk_norm + apply_rotary_emb / norm_rope
+ * (h3_inference/kernels/elementwise_norm_rope.py:19-40,104-148).
+ * D in {64, 128}; R even, R <= D, (R/2) % (D/32) == 0; row_stride, q_off,
+ * k_off multiples of 8.                                                    */
+H3B_API int h3b_qk_norm_rope(void* qkv, int64_t T, int64_t row_stride, int64_t q_off, int64_t k_off,
+                             int H, int D, const void* wq, const void* wk, float eps,
+                             const float* cos, const float* sin, int R, int64_t cs_stride,
+                             void* stream);
+
 /* ------------------------------------------------------------------ no-allocation variant
  * No counterpart in the reference.  The same RMSNorm(+modulation) -> NVFP4
  * result as h3b_rmsnorm_stats followed by h3b_rmsnorm_quantize (y_out not

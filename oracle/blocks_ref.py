@@ -60,3 +60,41 @@ def ffn_block(x, gamma, eps, w1q, b1, w2q, b2, gs_u=None):
     u, _ = nvfp4_linear_from_bf16(h, *w1q, bias=b1, act="gelu_tanh")
     y, gu = nvfp4_linear_from_bf16(u, *w2q, bias=b2, residual=x, gs_a=gs_u)
     return y, h, u
+
+
+def qk_norm_rope(x, w, eps, cos=None, sin=None) -> np.ndarray:
+    """Per-head RMSNorm over the last dim then rotate-half RoPE over the first
+    R = cos.shape[-1] dims (``h3_inference/kernels/elementwise_norm_rope.py:104-122``).
+    ``x``: [T, H, D]; ``cos``/``sin``: [T, R] (rounded to bf16 like the
+    reference's ``.to(xn.dtype)``).  fp64 math, one bf16 rounding."""
+    x = R.bf16_round(x).astype(np.float64)
+    if w is not None:
+        ms = np.mean(x * x, axis=-1, keepdims=True)
+        x = x / np.sqrt(ms + eps) * R.bf16_round(w).astype(np.float64)
+    if cos is not None:
+        rd = cos.shape[-1]
+        half = rd // 2
+        c = R.bf16_round(cos).astype(np.float64)[:, None, :]
+        s = R.bf16_round(sin).astype(np.float64)[:, None, :]
+        x1, x2 = x[..., :half], x[..., half:rd]
+        out = x.copy()
+        out[..., :half] = x1 * c[..., :half] - x2 * s[..., :half]
+        out[..., half:rd] = x2 * c[..., half:rd] + x1 * s[..., half:rd]
+        x = out
+    return R.bf16_round(x.astype(np.float32))
+
+
+def rope_tables(pos, dims, theta: float = 10000.0):
+    """(T, 3) positions -> fp32 (cos, sin) of shape (T, sum(dims)) for the
+    rotate-half layout ``H3RotaryPosEmbed`` builds
+    (``h3_inference/transformer/model.py:23-38``): first half = [t-axis |
+    h-axis | w-axis] angles, second half repeats it; generalised to per-axis
+    widths with per-axis inv_freq = theta^(-2i/d_axis)."""
+    pos = np.asarray(pos, dtype=np.float64)
+    freqs = []
+    for a, d in enumerate(dims):
+        inv = 1.0 / (theta ** (np.arange(0, d, 2, dtype=np.float64) / d))
+        freqs.append(pos[:, a:a + 1] * inv[None, :])
+    f = np.concatenate(freqs, axis=1)
+    f = np.concatenate([f, f], axis=1)
+    return np.cos(f).astype(np.float32), np.sin(f).astype(np.float32)
