@@ -19,6 +19,7 @@
 #include "gemm_nvfp4.cuh"
 #include "norm.cuh"
 #include "rope.cuh"
+#include "attention.cuh"
 
 namespace h3b {
 
@@ -423,6 +424,83 @@ int h3b_qk_norm_rope(void* qkv, int64_t T, int64_t row_stride, int64_t q_off, in
     k_qk_norm_rope<128><<<(unsigned)blocks, kRopeWarps * 32, 0, st>>>(a);
   else
     k_qk_norm_rope<64><<<(unsigned)blocks, kRopeWarps * 32, 0, st>>>(a);
+  return launched(cudaGetLastError());
+}
+
+// ------------------------------------------------------------------ packed varlen attention
+int h3b_attention_varlen(const void* qkv, int64_t T, int64_t row_stride, int64_t q_off,
+                         int64_t k_off, int64_t v_off, int H, int D,
+                         const int32_t* cu_seqlens_host, int ndocs, float scale, void* out,
+                         int64_t ldo, void* stream) {
+  if (T < 0 || H <= 0 || D != attn::D || ndocs <= 0 || ndocs > attn::MAX_DOCS || !cu_seqlens_host)
+    return H3B_ERR_INVALID_ARG;
+  if (!(scale > 0.f)) return H3B_ERR_INVALID_ARG;
+  if (cu_seqlens_host[0] != 0 || cu_seqlens_host[ndocs] != T) return H3B_ERR_INVALID_ARG;
+  for (int i = 0; i < ndocs; ++i)
+    if (cu_seqlens_host[i + 1] < cu_seqlens_host[i]) return H3B_ERR_INVALID_ARG;
+  const int64_t hd = (int64_t)H * D;
+  if (q_off < 0 || k_off < 0 || v_off < 0 || q_off + hd > row_stride || k_off + hd > row_stride ||
+      v_off + hd > row_stride || ldo < hd)
+    return H3B_ERR_INVALID_ARG;
+  if ((row_stride | q_off | k_off | v_off | ldo) % 8) return H3B_ERR_ALIGNMENT;
+  if (T > (int64_t)INT32_MAX - 256 || row_stride > (int64_t)INT32_MAX) return H3B_ERR_INVALID_ARG;
+  if (T == 0) return H3B_OK;
+  if (!qkv || !out) return H3B_ERR_INVALID_ARG;
+  if (!aligned16(qkv) || !aligned16(out)) return H3B_ERR_ALIGNMENT;
+  int rc = check_sm100();
+  if (rc != H3B_OK) return rc;
+
+  static std::once_flag attr_once;
+  static cudaError_t attr_err = cudaSuccess;
+  std::call_once(attr_once, [] {
+    attr_err = cudaFuncSetAttribute(attn::k_fmha, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    attn::SMEM_BYTES);
+  });
+  if (attr_err != cudaSuccess) return H3B_ERR_CUDA;
+
+  attn::Args args;
+  memset(&args, 0, sizeof(args));
+  CUtensorMap* tm = &args.tmap_qkv;
+  {
+    auto fn = encode_fn();
+    if (!fn) return H3B_ERR_UNSUPPORTED;
+    cuuint64_t dims[2] = {(cuuint64_t)row_stride, (cuuint64_t)T};
+    cuuint64_t strides[1] = {(cuuint64_t)row_stride * 2};
+    cuuint32_t box[2] = {64, attn::BK};
+    cuuint32_t estr[2] = {1, 1};
+    if (fn(tm, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(qkv), dims, strides, box, estr,
+           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+      return H3B_ERR_INVALID_ARG;
+  }
+  args.out = static_cast<__nv_bfloat16*>(out);
+  args.ldo = ldo;
+  args.q_off = (int)q_off;
+  args.k_off = (int)k_off;
+  args.v_off = (int)v_off;
+  args.H = H;
+  args.scale_log2 = scale * 1.4426950408889634f;
+  // longest documents first: they carry the most key tiles per CTA
+  int order[attn::MAX_DOCS];
+  int n = 0;
+  for (int i = 0; i < ndocs; ++i)
+    if (cu_seqlens_host[i + 1] > cu_seqlens_host[i]) order[n++] = i;
+  std::sort(order, order + n, [&](int a, int b) {
+    return cu_seqlens_host[a + 1] - cu_seqlens_host[a] > cu_seqlens_host[b + 1] - cu_seqlens_host[b];
+  });
+  int64_t items = 0;
+  for (int i = 0; i < n; ++i) {
+    const int d = order[i];
+    args.doc_start[i] = cu_seqlens_host[d];
+    args.doc_len[i] = cu_seqlens_host[d + 1] - cu_seqlens_host[d];
+    items += (int64_t)((args.doc_len[i] + attn::BQ - 1) / attn::BQ) * H;
+    if (items > INT32_MAX) return H3B_ERR_INVALID_ARG;
+    args.item_end[i] = (int)items;
+  }
+  args.ndocs = n;
+  if (items == 0) return H3B_OK;
+  attn::k_fmha<<<(unsigned)items, attn::THREADS, attn::SMEM_BYTES,
+                 static_cast<cudaStream_t>(stream)>>>(args);
   return launched(cudaGetLastError());
 }
 

@@ -211,3 +211,28 @@ def qk_norm_rope(qkv: torch.Tensor, heads: int, head_dim: int, *, q_off: int, k_
                                      _stream(dev))
     _lib.check(st, "h3b_qk_norm_rope")
     return qkv
+
+
+def attention_varlen(qkv: torch.Tensor, heads: int, head_dim: int, cu_seqlens, *, q_off: int,
+                     k_off: int, v_off: int, scale: float | None = None,
+                     out: torch.Tensor | None = None) -> torch.Tensor:
+    """Non-causal attention per document of a packed sequence, reading q/k/v
+    straight from the packed ``[T, row_stride]`` bf16 activation.  Returns
+    ``[T, heads*head_dim]`` bf16.  ``cu_seqlens``: host sequence of ndocs+1 ints."""
+    import ctypes
+
+    dev = _need_cuda(qkv, out)
+    q2 = qkv.reshape(-1, qkv.shape[-1]) if qkv.dim() != 2 else qkv
+    if q2.dtype != torch.bfloat16 or q2.stride(-1) != 1:
+        raise ValueError("qkv must be bf16 with a contiguous last dim")
+    T = q2.shape[0]
+    cu = [int(v) for v in (cu_seqlens.tolist() if hasattr(cu_seqlens, "tolist") else cu_seqlens)]
+    arr = (ctypes.c_int32 * len(cu))(*cu)
+    if out is None:
+        out = torch.empty(T, heads * head_dim, dtype=torch.bfloat16, device=dev)
+    sc = float(scale) if scale is not None else head_dim ** -0.5
+    st = _lib.lib().h3b_attention_varlen(_p(q2), T, q2.stride(0), q_off, k_off, v_off, heads,
+                                         head_dim, arr, len(cu) - 1, sc, _p(out), out.stride(0),
+                                         _stream(dev))
+    _lib.check(st, "h3b_attention_varlen")
+    return out

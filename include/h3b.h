@@ -144,6 +144,21 @@ H3B_API int h3b_qk_norm_rope(void* qkv, int64_t T, int64_t row_stride, int64_t q
                              const float* cos, const float* sin, int R, int64_t cs_stride,
                              void* stream);
 
+/* ------------------------------------------------------------------ packed varlen attention
+ * out[t, h*D + d] = softmax_j(q_t . k_j * scale) v_j over the keys j of the
+ * document that contains token t (non-causal), bf16 in/out, fp32 softmax.
+ * q / k / v head h are read from qkv[T, row_stride] at columns
+ * {q,k,v}_off + h*D (the packed QKV activation, after qk-norm + RoPE).
+ * cu_seqlens_host: HOST array of ndocs+1 document boundaries, [0] = 0,
+ * [ndocs] = T, non-decreasing (the launch shape depends on it); ndocs <= 64.
+ * D == 128.  Replaces F.scaled_dot_product_attention in packed_self_attention
+ * (h3_inference/kernels/packed_self_attn.py:8-37); cu_seqlens = {0, T}
+ * reproduces the reference's single-document attention.                    */
+H3B_API int h3b_attention_varlen(const void* qkv, int64_t T, int64_t row_stride, int64_t q_off,
+                                 int64_t k_off, int64_t v_off, int H, int D,
+                                 const int32_t* cu_seqlens_host, int ndocs, float scale,
+                                 void* out, int64_t ldo, void* stream);
+
 /* ------------------------------------------------------------------ no-allocation variant
  * No counterpart in the reference.  The same RMSNorm(+modulation) -> NVFP4
  * result as h3b_rmsnorm_stats followed by h3b_rmsnorm_quantize (y_out not

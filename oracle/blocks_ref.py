@@ -98,3 +98,27 @@ def rope_tables(pos, dims, theta: float = 10000.0):
     f = np.concatenate(freqs, axis=1)
     f = np.concatenate([f, f], axis=1)
     return np.cos(f).astype(np.float32), np.sin(f).astype(np.float32)
+
+
+def attention(q, k, v, cu_seqlens, scale: float | None = None, rows=None) -> np.ndarray:
+    """Non-causal softmax(q k^T * scale) v per document of a packed sequence
+    (``h3_inference/kernels/packed_self_attn.py:31-37`` with a per-document
+    mask).  ``q, k, v``: [T, H, D] (bf16 values); fp64 math, fp64 out.
+    ``rows`` optionally restricts the output to those query rows."""
+    q = np.asarray(q, dtype=np.float64)
+    k = np.asarray(k, dtype=np.float64)
+    v = np.asarray(v, dtype=np.float64)
+    T, H, D = q.shape
+    sc = D ** -0.5 if scale is None else scale
+    rows = np.arange(T) if rows is None else np.asarray(rows)
+    out = np.zeros((len(rows), H, D))
+    cu = list(cu_seqlens)
+    for i, r in enumerate(rows):
+        d = int(np.searchsorted(cu, r, side="right")) - 1
+        a, b = cu[d], cu[d + 1]
+        s = np.einsum("hd,jhd->hj", q[r], k[a:b]) * sc
+        s -= s.max(axis=1, keepdims=True)
+        p = np.exp(s)
+        p /= p.sum(axis=1, keepdims=True)
+        out[i] = np.einsum("hj,jhd->hd", p, v[a:b])
+    return out
