@@ -54,15 +54,18 @@ constexpr float kRescaleLog2 = 8.0f;
 static_assert(SMEM_BYTES <= 232448, "shared memory budget");
 
 struct Args {
-  CUtensorMap tmap_qkv;    // bf16 [T, row_stride], box 64 x 128, 128B swizzle
-  __nv_bfloat16* out;      // [T, ldo]; head h at columns h*D
+  CUtensorMap tmap_q;      // bf16 [q_rows, q_stride], box 64 x 128, 128B swizzle
+  CUtensorMap tmap_kv;     // bf16 [kv_rows, kv_stride], same box
+  __nv_bfloat16* out;      // [q_rows, ldo]; head h at columns h*D
   long long ldo;
-  int q_off, k_off, v_off; // element offsets of the q / k / v blocks in a row
+  int q_off, k_off, v_off; // element offsets of the q / k / v head blocks in their rows
   int H;
   float scale_log2;        // softmax scale * log2(e)
   int ndocs;
-  int doc_start[MAX_DOCS];
-  int doc_len[MAX_DOCS];
+  int doc_start[MAX_DOCS]; // first key row of the document (kv buffer rows)
+  int doc_len[MAX_DOCS];   // keys in the document
+  int q_start[MAX_DOCS];   // first local query row of the document (q buffer rows)
+  int q_len[MAX_DOCS];     // local queries in the document
   int item_end[MAX_DOCS];  // cumulative CTA counts (q_tiles * H) per document
 };
 
@@ -97,11 +100,12 @@ __global__ void __launch_bounds__(THREADS, 1) k_fmha(const __grid_constant__ Arg
   while (doc + 1 < p.ndocs && (int)blockIdx.x >= p.item_end[doc]) ++doc;
   const int item = (int)blockIdx.x - (doc > 0 ? p.item_end[doc - 1] : 0);
   const int len = p.doc_len[doc];
-  const int q_tiles = (len + BQ - 1) / BQ;
+  const int q_len = p.q_len[doc];
+  const int q_tiles = (q_len + BQ - 1) / BQ;
   const int head = item / q_tiles;
   const int qt = item - head * q_tiles;
   const int row0 = p.doc_start[doc];
-  const int q_row = row0 + qt * BQ;
+  const int q_row = p.q_start[doc] + qt * BQ;   // local row in the q / out buffers
   const int n_kv = (len + BK - 1) / BK;
 
   if (threadIdx.x == 0) {
@@ -139,12 +143,13 @@ __global__ void __launch_bounds__(THREADS, 1) k_fmha(const __grid_constant__ Arg
 
   if (warp == 0) {
     if (lane == 0) {
-      prefetch_tmap(&p.tmap_qkv);
+      prefetch_tmap(&p.tmap_q);
+      prefetch_tmap(&p.tmap_kv);
       const int qx = p.q_off + head * D, kx = p.k_off + head * D, vx = p.v_off + head * D;
       uint32_t fb = smem_u32(q_full);
       mbar_expect_tx(fb, TILE_BYTES);
-      tma_load_2d(smem_u32(smem + Q_OFF), &p.tmap_qkv, qx, q_row, fb);
-      tma_load_2d(smem_u32(smem + Q_OFF + BOX_BYTES), &p.tmap_qkv, qx + 64, q_row, fb);
+      tma_load_2d(smem_u32(smem + Q_OFF), &p.tmap_q, qx, q_row, fb);
+      tma_load_2d(smem_u32(smem + Q_OFF + BOX_BYTES), &p.tmap_q, qx + 64, q_row, fb);
       // issue order: K_0, then {K_{j+1}, V_j}: K runs one tile ahead of V
       int nk = 0, nv = 0;   // tiles issued
       bool ok = true;
@@ -154,8 +159,8 @@ __global__ void __launch_bounds__(THREADS, 1) k_fmha(const __grid_constant__ Arg
         const uint32_t b = smem_u32(&k_full[s]);
         mbar_expect_tx(b, TILE_BYTES);
         uint8_t* dst = smem + K_OFF + s * TILE_BYTES;
-        tma_load_2d(smem_u32(dst), &p.tmap_qkv, kx, row0 + j * BK, b);
-        tma_load_2d(smem_u32(dst + BOX_BYTES), &p.tmap_qkv, kx + 64, row0 + j * BK, b);
+        tma_load_2d(smem_u32(dst), &p.tmap_kv, kx, row0 + j * BK, b);
+        tma_load_2d(smem_u32(dst + BOX_BYTES), &p.tmap_kv, kx + 64, row0 + j * BK, b);
         ++nk;
         return true;
       };
@@ -165,8 +170,8 @@ __global__ void __launch_bounds__(THREADS, 1) k_fmha(const __grid_constant__ Arg
         const uint32_t b = smem_u32(&v_full[s]);
         mbar_expect_tx(b, TILE_BYTES);
         uint8_t* dst = smem + V_OFF + s * TILE_BYTES;
-        tma_load_2d(smem_u32(dst), &p.tmap_qkv, vx, row0 + j * BK, b);
-        tma_load_2d(smem_u32(dst + BOX_BYTES), &p.tmap_qkv, vx + 64, row0 + j * BK, b);
+        tma_load_2d(smem_u32(dst), &p.tmap_kv, vx, row0 + j * BK, b);
+        tma_load_2d(smem_u32(dst + BOX_BYTES), &p.tmap_kv, vx + 64, row0 + j * BK, b);
         ++nv;
         return true;
       };
@@ -320,7 +325,7 @@ __global__ void __launch_bounds__(THREADS, 1) k_fmha(const __grid_constant__ Arg
     } else if (n_kv > 0) {
       tc_fence_after();
       const float inv_l = 1.0f / l;
-      const bool row_ok = qt * BQ + r < len;
+      const bool row_ok = qt * BQ + r < q_len;
       __nv_bfloat16* op = p.out + (size_t)(q_row + r) * p.ldo + (size_t)head * D;
 #pragma unroll
       for (int h = 0; h < 2; ++h) {

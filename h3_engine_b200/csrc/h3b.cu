@@ -428,25 +428,43 @@ int h3b_qk_norm_rope(void* qkv, int64_t T, int64_t row_stride, int64_t q_off, in
 }
 
 // ------------------------------------------------------------------ packed varlen attention
-int h3b_attention_varlen(const void* qkv, int64_t T, int64_t row_stride, int64_t q_off,
+static int tmap_bf16_rows(CUtensorMap* tm, const void* base, int64_t rows, int64_t stride) {
+  auto fn = encode_fn();
+  if (!fn) return H3B_ERR_UNSUPPORTED;
+  cuuint64_t dims[2] = {(cuuint64_t)stride, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)stride * 2};
+  cuuint32_t box[2] = {64, attn::BK};
+  cuuint32_t estr[2] = {1, 1};
+  return fn(tm, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box,
+            estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS
+             ? H3B_OK
+             : H3B_ERR_INVALID_ARG;
+}
+
+int h3b_attention_varlen(const void* q_buf, int64_t q_rows, int64_t q_stride, int64_t q_off,
+                         int64_t q_row0, const void* kv_buf, int64_t kv_rows, int64_t kv_stride,
                          int64_t k_off, int64_t v_off, int H, int D,
                          const int32_t* cu_seqlens_host, int ndocs, float scale, void* out,
                          int64_t ldo, void* stream) {
-  if (T < 0 || H <= 0 || D != attn::D || ndocs <= 0 || ndocs > attn::MAX_DOCS || !cu_seqlens_host)
+  if (q_rows < 0 || kv_rows < 0 || q_row0 < 0 || q_row0 + q_rows > kv_rows) return H3B_ERR_INVALID_ARG;
+  if (H <= 0 || D != attn::D || ndocs <= 0 || ndocs > attn::MAX_DOCS || !cu_seqlens_host)
     return H3B_ERR_INVALID_ARG;
   if (!(scale > 0.f)) return H3B_ERR_INVALID_ARG;
-  if (cu_seqlens_host[0] != 0 || cu_seqlens_host[ndocs] != T) return H3B_ERR_INVALID_ARG;
+  if (cu_seqlens_host[0] != 0 || cu_seqlens_host[ndocs] != kv_rows) return H3B_ERR_INVALID_ARG;
   for (int i = 0; i < ndocs; ++i)
     if (cu_seqlens_host[i + 1] < cu_seqlens_host[i]) return H3B_ERR_INVALID_ARG;
   const int64_t hd = (int64_t)H * D;
-  if (q_off < 0 || k_off < 0 || v_off < 0 || q_off + hd > row_stride || k_off + hd > row_stride ||
-      v_off + hd > row_stride || ldo < hd)
+  if (q_off < 0 || k_off < 0 || v_off < 0 || q_off + hd > q_stride || k_off + hd > kv_stride ||
+      v_off + hd > kv_stride || ldo < hd)
     return H3B_ERR_INVALID_ARG;
-  if ((row_stride | q_off | k_off | v_off | ldo) % 8) return H3B_ERR_ALIGNMENT;
-  if (T > (int64_t)INT32_MAX - 256 || row_stride > (int64_t)INT32_MAX) return H3B_ERR_INVALID_ARG;
-  if (T == 0) return H3B_OK;
-  if (!qkv || !out) return H3B_ERR_INVALID_ARG;
-  if (!aligned16(qkv) || !aligned16(out)) return H3B_ERR_ALIGNMENT;
+  if ((q_stride | kv_stride | q_off | k_off | v_off | ldo) % 8) return H3B_ERR_ALIGNMENT;
+  if (kv_rows > (int64_t)INT32_MAX - 256 || q_stride > (int64_t)INT32_MAX ||
+      kv_stride > (int64_t)INT32_MAX)
+    return H3B_ERR_INVALID_ARG;
+  if (q_rows == 0) return H3B_OK;
+  if (!q_buf || !kv_buf || !out) return H3B_ERR_INVALID_ARG;
+  if (!aligned16(q_buf) || !aligned16(kv_buf) || !aligned16(out)) return H3B_ERR_ALIGNMENT;
   int rc = check_sm100();
   if (rc != H3B_OK) return rc;
 
@@ -460,19 +478,10 @@ int h3b_attention_varlen(const void* qkv, int64_t T, int64_t row_stride, int64_t
 
   attn::Args args;
   memset(&args, 0, sizeof(args));
-  CUtensorMap* tm = &args.tmap_qkv;
-  {
-    auto fn = encode_fn();
-    if (!fn) return H3B_ERR_UNSUPPORTED;
-    cuuint64_t dims[2] = {(cuuint64_t)row_stride, (cuuint64_t)T};
-    cuuint64_t strides[1] = {(cuuint64_t)row_stride * 2};
-    cuuint32_t box[2] = {64, attn::BK};
-    cuuint32_t estr[2] = {1, 1};
-    if (fn(tm, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(qkv), dims, strides, box, estr,
-           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
-      return H3B_ERR_INVALID_ARG;
-  }
+  rc = tmap_bf16_rows(&args.tmap_q, q_buf, q_rows, q_stride);
+  if (rc != H3B_OK) return rc;
+  rc = tmap_bf16_rows(&args.tmap_kv, kv_buf, kv_rows, kv_stride);
+  if (rc != H3B_OK) return rc;
   args.out = static_cast<__nv_bfloat16*>(out);
   args.ldo = ldo;
   args.q_off = (int)q_off;
@@ -480,20 +489,27 @@ int h3b_attention_varlen(const void* qkv, int64_t T, int64_t row_stride, int64_t
   args.v_off = (int)v_off;
   args.H = H;
   args.scale_log2 = scale * 1.4426950408889634f;
-  // longest documents first: they carry the most key tiles per CTA
+  // documents that own local queries; longest key ranges first (most work per CTA)
   int order[attn::MAX_DOCS];
   int n = 0;
-  for (int i = 0; i < ndocs; ++i)
-    if (cu_seqlens_host[i + 1] > cu_seqlens_host[i]) order[n++] = i;
+  for (int i = 0; i < ndocs; ++i) {
+    const int64_t a = std::max<int64_t>(cu_seqlens_host[i], q_row0);
+    const int64_t b = std::min<int64_t>(cu_seqlens_host[i + 1], q_row0 + q_rows);
+    if (b > a) order[n++] = i;
+  }
   std::sort(order, order + n, [&](int a, int b) {
     return cu_seqlens_host[a + 1] - cu_seqlens_host[a] > cu_seqlens_host[b + 1] - cu_seqlens_host[b];
   });
   int64_t items = 0;
   for (int i = 0; i < n; ++i) {
     const int d = order[i];
+    const int64_t qa = std::max<int64_t>(cu_seqlens_host[d], q_row0);
+    const int64_t qb = std::min<int64_t>(cu_seqlens_host[d + 1], q_row0 + q_rows);
     args.doc_start[i] = cu_seqlens_host[d];
     args.doc_len[i] = cu_seqlens_host[d + 1] - cu_seqlens_host[d];
-    items += (int64_t)((args.doc_len[i] + attn::BQ - 1) / attn::BQ) * H;
+    args.q_start[i] = (int)(qa - q_row0);
+    args.q_len[i] = (int)(qb - qa);
+    items += (int64_t)((args.q_len[i] + attn::BQ - 1) / attn::BQ) * H;
     if (items > INT32_MAX) return H3B_ERR_INVALID_ARG;
     args.item_end[i] = (int)items;
   }

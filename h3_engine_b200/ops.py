@@ -215,23 +215,32 @@ def qk_norm_rope(qkv: torch.Tensor, heads: int, head_dim: int, *, q_off: int, k_
 
 def attention_varlen(qkv: torch.Tensor, heads: int, head_dim: int, cu_seqlens, *, q_off: int,
                      k_off: int, v_off: int, scale: float | None = None,
-                     out: torch.Tensor | None = None) -> torch.Tensor:
-    """Non-causal attention per document of a packed sequence, reading q/k/v
-    straight from the packed ``[T, row_stride]`` bf16 activation.  Returns
-    ``[T, heads*head_dim]`` bf16.  ``cu_seqlens``: host sequence of ndocs+1 ints."""
+                     out: torch.Tensor | None = None, kv: torch.Tensor | None = None,
+                     q_row0: int = 0) -> torch.Tensor:
+    """Non-causal attention per document of a packed sequence.
+
+    ``qkv``: bf16 ``[rows, stride]`` holding the query heads at ``q_off``
+    (and, when ``kv`` is None, the key / value heads at ``k_off`` / ``v_off``).
+    ``kv``: optional bf16 ``[T, stride]`` with the keys / values of the whole
+    sequence (token-sharded runs: ``qkv`` is the local shard whose first row is
+    global row ``q_row0``).  ``cu_seqlens``: host sequence of global document
+    boundaries.  Returns ``[rows, heads*head_dim]`` bf16."""
     import ctypes
 
-    dev = _need_cuda(qkv, out)
+    dev = _need_cuda(qkv, out, kv)
     q2 = qkv.reshape(-1, qkv.shape[-1]) if qkv.dim() != 2 else qkv
-    if q2.dtype != torch.bfloat16 or q2.stride(-1) != 1:
-        raise ValueError("qkv must be bf16 with a contiguous last dim")
-    T = q2.shape[0]
+    kv2 = q2 if kv is None else (kv.reshape(-1, kv.shape[-1]) if kv.dim() != 2 else kv)
+    for t in (q2, kv2):
+        if t.dtype != torch.bfloat16 or t.stride(-1) != 1:
+            raise ValueError("q / kv buffers must be bf16 with a contiguous last dim")
+    rows = q2.shape[0]
     cu = [int(v) for v in (cu_seqlens.tolist() if hasattr(cu_seqlens, "tolist") else cu_seqlens)]
     arr = (ctypes.c_int32 * len(cu))(*cu)
     if out is None:
-        out = torch.empty(T, heads * head_dim, dtype=torch.bfloat16, device=dev)
+        out = torch.empty(rows, heads * head_dim, dtype=torch.bfloat16, device=dev)
     sc = float(scale) if scale is not None else head_dim ** -0.5
-    st = _lib.lib().h3b_attention_varlen(_p(q2), T, q2.stride(0), q_off, k_off, v_off, heads,
+    st = _lib.lib().h3b_attention_varlen(_p(q2), rows, q2.stride(0), q_off, q_row0, _p(kv2),
+                                         kv2.shape[0], kv2.stride(0), k_off, v_off, heads,
                                          head_dim, arr, len(cu) - 1, sc, _p(out), out.stride(0),
                                          _stream(dev))
     _lib.check(st, "h3b_attention_varlen")

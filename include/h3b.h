@@ -145,17 +145,23 @@ H3B_API int h3b_qk_norm_rope(void* qkv, int64_t T, int64_t row_stride, int64_t q
                              void* stream);
 
 /* ------------------------------------------------------------------ packed varlen attention
- * out[t, h*D + d] = softmax_j(q_t . k_j * scale) v_j over the keys j of the
- * document that contains token t (non-causal), bf16 in/out, fp32 softmax.
- * q / k / v head h are read from qkv[T, row_stride] at columns
- * {q,k,v}_off + h*D (the packed QKV activation, after qk-norm + RoPE).
- * cu_seqlens_host: HOST array of ndocs+1 document boundaries, [0] = 0,
- * [ndocs] = T, non-decreasing (the launch shape depends on it); ndocs <= 64.
- * D == 128.  Replaces F.scaled_dot_product_attention in packed_self_attention
+ * out[i, h*D + d] = softmax_j(q_i . k_j * scale) v_j for every local query row
+ * i, over the keys j of the document that contains its global row q_row0 + i
+ * (non-causal), bf16 in/out, fp32 softmax and accumulation.
+ *   q head h: q_buf[i, q_off + h*D .. +D)       (q_rows rows, row stride q_stride)
+ *   k / v head h: kv_buf[j, {k,v}_off + h*D ..) (kv_rows rows = the full sequence)
+ * With q_buf == kv_buf, q_row0 = 0 and q_rows = kv_rows this is plain packed
+ * attention over one QKV activation; with a token-sharded sequence q_buf is
+ * the local shard and kv_buf the gathered keys / values.
+ * cu_seqlens_host: HOST array of ndocs+1 global document boundaries, [0] = 0,
+ * [ndocs] = kv_rows, non-decreasing (the launch shape depends on it);
+ * ndocs <= 64; D == 128; strides / offsets multiples of 8.
+ * Replaces F.scaled_dot_product_attention in packed_self_attention
  * (h3_inference/kernels/packed_self_attn.py:8-37); cu_seqlens = {0, T}
  * reproduces the reference's single-document attention.                    */
-H3B_API int h3b_attention_varlen(const void* qkv, int64_t T, int64_t row_stride, int64_t q_off,
-                                 int64_t k_off, int64_t v_off, int H, int D,
+H3B_API int h3b_attention_varlen(const void* q_buf, int64_t q_rows, int64_t q_stride, int64_t q_off,
+                                 int64_t q_row0, const void* kv_buf, int64_t kv_rows,
+                                 int64_t kv_stride, int64_t k_off, int64_t v_off, int H, int D,
                                  const int32_t* cu_seqlens_host, int ndocs, float scale,
                                  void* out, int64_t ldo, void* stream);
 
