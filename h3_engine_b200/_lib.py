@@ -30,8 +30,8 @@ SIGNATURES: dict[str, tuple] = {
                                     _c_void_p, _c_void_p]),
     "h3b_nvfp4_gemm": (_i32, [_c_void_p, _c_void_p, _c_void_p, _i64, _i64,
                               _c_void_p, _c_void_p, _c_void_p, _i64, _i64, _i64,
-                              _c_void_p, _c_void_p, _i64, _i32, _c_void_p, _i64, _c_void_p,
-                              _c_void_p]),
+                              _c_void_p, _c_void_p, _i64, _c_void_p, _c_void_p, _i32, _c_void_p,
+                              _i64, _c_void_p, _c_void_p]),
     "h3b_rmsnorm_stats": (_i32, [_c_void_p, _i64, _i64, _i64, _c_void_p, _f32, _c_void_p,
                                  _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p]),
     "h3b_rmsnorm_quantize": (_i32, [_c_void_p, _i64, _i64, _i64, _c_void_p, _c_void_p, _c_void_p,

@@ -4,282 +4,11 @@
 // h3_inference/nvfp4.py:112-115 together with the bias / GELU / residual work
 // that follows it in the row shims (h3_inference/kernels/ffn_qkvo_gemms.py).
 //
-// One CTA computes a 128 x 256 output tile:
-//   warp 0      TMA producer: A tile 128 x 128 B, B tile 256 x 128 B (both
-//               128-byte swizzled), and the scale-factor atoms of this k-block
-//               by bulk copy (the global scale layout IS the 512-byte atom the
-//               tensor core reads, so no reshuffle is needed);
-//   warp 1      allocates tensor memory, then one thread copies the scale
-//               atoms smem->TMEM (tcgen05.cp) and issues
-//               tcgen05.mma.kind::mxf4nvf4.block_scale (M=128, N=256, K=64);
-//   warps 2..5  epilogue: TMEM -> registers (tcgen05.ld), alpha = gsA*gsB,
-//               bias, GELU-tanh, residual, bf16 store, |D| max for re-quant.
-// k-block = 256 E2M1 values (128 bytes per row, one swizzle row), 4 stages.
-// TMEM: accumulator columns [0,256), scale factors [256, 256+4*48).
 #pragma once
 
 #include "common.cuh"
 
 namespace h3b {
-namespace gemm_v1 {
-
-constexpr int BM = 128;
-constexpr int BN = 256;
-constexpr int KB_ELEMS = 256;            // E2M1 values per k-block
-constexpr int KB_BYTES = KB_ELEMS / 2;   // 128
-constexpr int STAGES = 4;
-constexpr int A_BYTES = BM * KB_BYTES;   // 16 KiB
-constexpr int B_BYTES = BN * KB_BYTES;   // 32 KiB
-constexpr int SF_ATOM = 512;             // 128 rows x 4 scales
-constexpr int SFA_BYTES = (BM / 128) * 4 * SF_ATOM;   // 2 KiB
-constexpr int SFB_BYTES = (BN / 128) * 4 * SF_ATOM;   // 4 KiB
-constexpr int STAGE_BYTES = A_BYTES + B_BYTES + SFA_BYTES + SFB_BYTES;  // 54 KiB
-constexpr int BAR_BYTES = 256;
-constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + BAR_BYTES + 1024;
-constexpr int THREADS = 192;
-constexpr uint32_t TMEM_COLS = 512;
-constexpr uint32_t ACC_COL = 0;
-constexpr uint32_t SF_COL = 256;
-constexpr uint32_t SF_STAGE_COLS = 4 * 4 + 4 * 8;   // per k-block: SFA 4 MMAs x 4 cols, SFB x 8
-// Instruction descriptor, kind::mxf4nvf4: A,B = E2M1 (1), scales = ue4m3 (0),
-// K-major A and B, N>>3 at bit 17, M>>4 at bit 24, dense K = 64.
-constexpr uint32_t IDESC = (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) |
-                           ((uint32_t)(BM >> 4) << 24);
-
-static_assert(STAGE_BYTES % 1024 == 0, "stage must keep 1024-byte swizzle alignment");
-static_assert(SF_COL + STAGES * SF_STAGE_COLS <= TMEM_COLS, "TMEM budget");
-
-struct Args {
-  CUtensorMap tmap_a;      // u8 [a_rows, K/2], box 128 x 128, 128B swizzle
-  CUtensorMap tmap_b;      // u8 [N, K/2],      box 128 x 256, 128B swizzle
-  const uint8_t* sfa;      // swizzled scales of A
-  const uint8_t* sfb;      // swizzled scales of B
-  const float* gs_a;
-  const float* gs_b;
-  const __nv_bfloat16* bias;
-  const __nv_bfloat16* residual;
-  __nv_bfloat16* d;
-  float* amax_out;
-  long long ldr;
-  long long ldd;
-  int M, N, K;
-  int sf_atoms_k;          // K / 64: scale atoms per 128-row block
-  int act;
-  int gsb_seg;             // columns per gs_b entry (0: gs_b is one scalar)
-};
-
-__device__ __forceinline__ float gelu_tanh(float v) {
-  // 0.5 v (1 + tanh(sqrt(2/pi) (v + 0.044715 v^3))), tanh from the hardware
-  // tanh.approx.f32 instruction (max relative error ~2^-11, below bf16 ulp).
-  const float u = 0.7978845608028654f * fmaf(0.044715f * v, v * v, v);
-  float t;
-  asm("tanh.approx.f32 %0, %1;" : "=f"(t) : "f"(u));
-  return 0.5f * v * (1.0f + t);
-}
-
-__global__ void __launch_bounds__(THREADS, 1) k_gemm_nvfp4(const __grid_constant__ Args p) {
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
-                                             ~uintptr_t(1023));
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
-  uint64_t* full = bars;
-  uint64_t* empty = bars + STAGES;
-  uint64_t* acc_full = bars + 2 * STAGES;
-  uint64_t* drain = bars + 2 * STAGES + 1;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 2);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int m0 = blockIdx.y * BM, n0 = blockIdx.x * BN;
-  const int num_kb = p.K / KB_ELEMS;
-  const bool b_hi = (n0 + 128) < p.N;   // second 128-row half of the B tile exists
-
-  auto sA = [&](int s) { return smem + s * STAGE_BYTES; };
-  auto sB = [&](int s) { return smem + s * STAGE_BYTES + A_BYTES; };
-  auto sSFA = [&](int s) { return smem + s * STAGE_BYTES + A_BYTES + B_BYTES; };
-  auto sSFB = [&](int s) { return smem + s * STAGE_BYTES + A_BYTES + B_BYTES + SFA_BYTES; };
-
-  if (threadIdx.x == 0) {
-    for (int s = 0; s < STAGES; ++s) {
-      mbar_init(smem_u32(&full[s]), 1);
-      mbar_init(smem_u32(&empty[s]), 1);
-    }
-    mbar_init(smem_u32(acc_full), 1);
-    mbar_init(smem_u32(drain), 1);
-    *abort_flag = 0;
-    fence_mbar_init();
-  }
-  if (warp == 1) {
-    tmem_alloc(smem_u32(tmem_slot), TMEM_COLS);
-    tmem_relinquish();
-  }
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  const uint32_t tmem = *tmem_slot;
-
-  if (warp == 0) {
-    if (lane == 0) {
-      prefetch_tmap(&p.tmap_a);
-      prefetch_tmap(&p.tmap_b);
-      const uint32_t tx = A_BYTES + B_BYTES + SFA_BYTES + (b_hi ? 2 : 1) * 4 * SF_ATOM;
-      const uint8_t* sfa_row = p.sfa + (size_t)(m0 / 128) * p.sf_atoms_k * SF_ATOM;
-      const uint8_t* sfb_row0 = p.sfb + (size_t)(n0 / 128) * p.sf_atoms_k * SF_ATOM;
-      const uint8_t* sfb_row1 = sfb_row0 + (size_t)p.sf_atoms_k * SF_ATOM;
-      int issued = 0;
-      for (int kb = 0; kb < num_kb; ++kb) {
-        const int s = kb % STAGES;
-        const uint32_t ph = (kb / STAGES) & 1;
-        if (kb >= STAGES && !mbar_wait(smem_u32(&empty[s]), ph ^ 1, abort_flag)) {
-          record_error(H3B_ERR_TIMEOUT);
-          *abort_flag = 1;
-          break;
-        }
-        const uint32_t fb = smem_u32(&full[s]);
-        mbar_expect_tx(fb, tx);
-        tma_load_2d(smem_u32(sA(s)), &p.tmap_a, kb * KB_BYTES, m0, fb);
-        tma_load_2d(smem_u32(sB(s)), &p.tmap_b, kb * KB_BYTES, n0, fb);
-        bulk_load(smem_u32(sSFA(s)), sfa_row + (size_t)kb * 4 * SF_ATOM, 4 * SF_ATOM, fb);
-        bulk_load(smem_u32(sSFB(s)), sfb_row0 + (size_t)kb * 4 * SF_ATOM, 4 * SF_ATOM, fb);
-        if (b_hi)
-          bulk_load(smem_u32(sSFB(s)) + 4 * SF_ATOM, sfb_row1 + (size_t)kb * 4 * SF_ATOM,
-                    4 * SF_ATOM, fb);
-        ++issued;
-      }
-      if (*abort_flag) {
-        // Let every copy already in flight land before the CTA can exit.
-        for (int kb = issued > STAGES ? issued - STAGES : 0; kb < issued; ++kb)
-          mbar_wait(smem_u32(&full[kb % STAGES]), (kb / STAGES) & 1, nullptr);
-      }
-    }
-  } else if (warp == 1) {
-    if (lane == 0) {
-      int kb = 0;
-      for (; kb < num_kb; ++kb) {
-        const int s = kb % STAGES;
-        const uint32_t ph = (kb / STAGES) & 1;
-        if (!mbar_wait(smem_u32(&full[s]), ph, abort_flag)) {
-          record_error(H3B_ERR_TIMEOUT);
-          *abort_flag = 1;
-          break;
-        }
-        tc_fence_after();
-        const uint32_t sf_t = tmem + SF_COL + s * SF_STAGE_COLS;
-        const uint32_t sfa_s = smem_u32(sSFA(s));
-        const uint32_t sfb_s = smem_u32(sSFB(s));
-#pragma unroll
-        for (int kk = 0; kk < 4; ++kk) {
-          tc_cp_32x128b_warpx4(sf_t + kk * 4, desc_sf_atom(sfa_s + kk * SF_ATOM));
-          tc_cp_32x128b_warpx4(sf_t + 16 + kk * 8, desc_sf_atom(sfb_s + kk * SF_ATOM));
-          tc_cp_32x128b_warpx4(sf_t + 16 + kk * 8 + 4,
-                               desc_sf_atom(sfb_s + 4 * SF_ATOM + kk * SF_ATOM));
-        }
-        const uint32_t a_s = smem_u32(sA(s)), b_s = smem_u32(sB(s));
-#pragma unroll
-        for (int kk = 0; kk < 4; ++kk) {
-          tc_mma_nvf4(tmem + ACC_COL, desc_kmajor_sw128(a_s + kk * 32),
-                      desc_kmajor_sw128(b_s + kk * 32), IDESC, sf_t + kk * 4, sf_t + 16 + kk * 8,
-                      (kb | kk) != 0);
-        }
-        tc_commit(smem_u32(&empty[s]));
-      }
-      if (kb == num_kb) {
-        tc_commit(smem_u32(acc_full));
-      } else {
-        // Unwind: make sure no tensor-core op still reads smem / writes TMEM.
-        tc_commit(smem_u32(drain));
-        mbar_wait(smem_u32(drain), 0, nullptr);
-      }
-    }
-  } else {
-    // Epilogue: warp w may only touch TMEM lanes [32*(w%4), 32*(w%4)+32).
-    const int qd = warp & 3;
-    const int row = m0 + qd * 32 + lane;
-    const bool acc_ready = __all_sync(0xffffffffu, mbar_wait(smem_u32(acc_full), 0, abort_flag));
-    if (!acc_ready) {
-      if (!*abort_flag) {
-        record_error(H3B_ERR_TIMEOUT);
-        *abort_flag = 1;
-      }
-    } else {
-      tc_fence_after();
-      const float gsa = p.gs_a ? __ldg(p.gs_a) : 1.f;
-      float amax = 0.f;
-      const bool row_ok = row < p.M;
-#pragma unroll 1
-      for (int c = 0; c < BN / 32; ++c) {
-        __syncwarp();
-        uint32_t r[32];
-        tmem_ld_32x32b_x32(tmem + ACC_COL + ((uint32_t)(qd * 32) << 16) + c * 32, r);
-        tmem_ld_wait();
-        const int n = n0 + c * 32;
-        if (row_ok && n < p.N) {
-          const float alpha =
-              gsa * (p.gs_b ? __ldg(p.gs_b + (p.gsb_seg ? n / p.gsb_seg : 0)) : 1.f);
-          float v[32];
-#pragma unroll
-          for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]) * alpha;
-          if (p.bias) {
-            const uint4* bp = reinterpret_cast<const uint4*>(p.bias + n);
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-              const uint4 b = __ldg(bp + j);
-              const uint32_t bw[4] = {b.x, b.y, b.z, b.w};
-#pragma unroll
-              for (int t = 0; t < 4; ++t) {
-                v[8 * j + 2 * t] += __uint_as_float(bw[t] << 16);
-                v[8 * j + 2 * t + 1] += __uint_as_float(bw[t] & 0xFFFF0000u);
-              }
-            }
-          }
-          if (p.act == H3B_ACT_GELU_TANH) {
-#pragma unroll
-            for (int i = 0; i < 32; ++i) v[i] = gelu_tanh(v[i]);
-          }
-          if (p.residual) {
-            const uint4* rp = reinterpret_cast<const uint4*>(p.residual + (size_t)row * p.ldr + n);
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-              const uint4 b = __ldg(rp + j);
-              const uint32_t bw[4] = {b.x, b.y, b.z, b.w};
-#pragma unroll
-              for (int t = 0; t < 4; ++t) {
-                v[8 * j + 2 * t] += __uint_as_float(bw[t] << 16);
-                v[8 * j + 2 * t + 1] += __uint_as_float(bw[t] & 0xFFFF0000u);
-              }
-            }
-          }
-          uint32_t o[16];
-#pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            o[i] = pack_bf16x2(v[2 * i], v[2 * i + 1]);
-            amax = fmaxf(amax, fabsf(__uint_as_float(o[i] << 16)));
-            amax = fmaxf(amax, fabsf(__uint_as_float(o[i] & 0xFFFF0000u)));
-          }
-          uint4* dp = reinterpret_cast<uint4*>(p.d + (size_t)row * p.ldd + n);
-#pragma unroll
-          for (int j = 0; j < 4; ++j) dp[j] = make_uint4(o[4 * j], o[4 * j + 1], o[4 * j + 2], o[4 * j + 3]);
-        }
-      }
-      if (p.amax_out) {
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-        if (lane == 0 && amax > 0.f)
-          atomicMax(reinterpret_cast<unsigned int*>(p.amax_out), __float_as_uint(amax));
-      }
-    }
-  }
-
-  tc_fence_before();
-  __syncthreads();
-  if (warp == 1) {
-    __syncwarp();
-    tc_fence_after();
-    tmem_dealloc(tmem, TMEM_COLS);
-  }
-}
-
-}  // namespace gemm_v1
 
 // ============================================================================
 // Persistent variant (the production kernel).
@@ -341,6 +70,8 @@ struct Args {
   const float* gs_b;
   const __nv_bfloat16* bias;
   const __nv_bfloat16* residual;
+  const __nv_bfloat16* gate;   // [rows, N]: v *= gate[gate_idx[m], n] (adaLN-zero gate)
+  const int32_t* gate_idx;     // [M] or null (row 0)
   float* amax_out;
   long long ldr;
   int M, N, K;
@@ -351,7 +82,14 @@ struct Args {
   int num_tiles;
 };
 
-__device__ __forceinline__ float gelu_tanh(float v) { return gemm_v1::gelu_tanh(v); }
+__device__ __forceinline__ float gelu_tanh(float v) {
+  // 0.5 v (1 + tanh(sqrt(2/pi) (v + 0.044715 v^3))), tanh from the hardware
+  // tanh.approx.f32 instruction (max relative error ~2^-11, below bf16 ulp).
+  const float u = 0.7978845608028654f * fmaf(0.044715f * v, v * v, v);
+  float t;
+  asm("tanh.approx.f32 %0, %1;" : "=f"(t) : "f"(u));
+  return 0.5f * v * (1.0f + t);
+}
 
 __global__ void __launch_bounds__(THREADS, 1) k_gemm_nvfp4(const __grid_constant__ Args p) {
   extern __shared__ uint8_t smem_raw[];
@@ -542,6 +280,16 @@ __global__ void __launch_bounds__(THREADS, 1) k_gemm_nvfp4(const __grid_constant
             if (p.act == H3B_ACT_GELU_TANH) {
 #pragma unroll
               for (int e = 0; e < 8; ++e) v[e] = gelu_tanh(v[e]);
+            }
+            if (p.gate) {
+              const long long grow = p.gate_idx ? (row_ok ? __ldg(p.gate_idx + row) : 0) : 0;
+              const uint4 b = __ldg(reinterpret_cast<const uint4*>(p.gate + grow * p.N + col));
+              const uint32_t bw[4] = {b.x, b.y, b.z, b.w};
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                v[2 * e] *= __uint_as_float(bw[e] << 16);
+                v[2 * e + 1] *= __uint_as_float(bw[e] & 0xFFFF0000u);
+              }
             }
             if (p.residual && row_ok) {
               const uint4 b =

@@ -104,52 +104,6 @@ static int make_tmap_bf16_sw128(CUtensorMap* map, const void* base, uint64_t row
 
 using namespace h3b;
 
-// The first (non-persistent, one tile per CTA) GEMM kernel, kept selectable
-// with H3B_GEMM_V1=1 for A/B timing against the persistent kernel.
-static int gemm_v1_launch(const void* A, const void* sfA, const float* gsA, int64_t M,
-                          int64_t a_rows, const void* B, const void* sfB, const float* gsB,
-                          int64_t gsb_seg, int64_t N, int64_t K, const void* bias,
-                          const void* residual, int64_t ldr, int act, void* D, int64_t ldd,
-                          float* amax_out, void* stream) {
-  static std::once_flag attr_once;
-  static cudaError_t attr_err = cudaSuccess;
-  std::call_once(attr_once, [] {
-    attr_err = cudaFuncSetAttribute(gemm_v1::k_gemm_nvfp4,
-                                    cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                    gemm_v1::SMEM_BYTES);
-  });
-  if (attr_err != cudaSuccess) return H3B_ERR_CUDA;
-  gemm_v1::Args args;
-  memset(&args, 0, sizeof(args));
-  int rc = make_tmap_u8_sw128(&args.tmap_a, A, (uint64_t)a_rows, (uint64_t)(K / 2),
-                              (uint64_t)(K / 2), gemm_v1::KB_BYTES, gemm_v1::BM);
-  if (rc != H3B_OK) return rc;
-  rc = make_tmap_u8_sw128(&args.tmap_b, B, (uint64_t)N, (uint64_t)(K / 2), (uint64_t)(K / 2),
-                          gemm_v1::KB_BYTES, gemm_v1::BN);
-  if (rc != H3B_OK) return rc;
-  args.sfa = static_cast<const uint8_t*>(sfA);
-  args.sfb = static_cast<const uint8_t*>(sfB);
-  args.gs_a = gsA;
-  args.gs_b = gsB;
-  args.bias = static_cast<const __nv_bfloat16*>(bias);
-  args.residual = static_cast<const __nv_bfloat16*>(residual);
-  args.d = static_cast<__nv_bfloat16*>(D);
-  args.amax_out = amax_out;
-  args.ldr = residual ? ldr : 0;
-  args.ldd = ldd;
-  args.M = (int)M;
-  args.N = (int)N;
-  args.K = (int)K;
-  args.sf_atoms_k = (int)(K / 64);
-  args.act = act;
-  args.gsb_seg = (int)gsb_seg;
-  dim3 grid((unsigned)((N + gemm_v1::BN - 1) / gemm_v1::BN),
-            (unsigned)((M + gemm_v1::BM - 1) / gemm_v1::BM));
-  gemm_v1::k_gemm_nvfp4<<<grid, gemm_v1::THREADS, gemm_v1::SMEM_BYTES,
-                          static_cast<cudaStream_t>(stream)>>>(args);
-  return launched(cudaGetLastError());
-}
-
 extern "C" {
 
 int h3b_version(void) { return 1; }
@@ -258,9 +212,11 @@ int h3b_nvfp4_dequantize(const void* q, const void* sf, int sf_layout, int64_t s
 // ------------------------------------------------------------------ GEMM
 int h3b_nvfp4_gemm(const void* A, const void* sfA, const float* gsA, int64_t M, int64_t a_rows,
                    const void* B, const void* sfB, const float* gsB, int64_t gsb_seg, int64_t N,
-                   int64_t K, const void* bias, const void* residual, int64_t ldr, int act,
-                   void* D, int64_t ldd, float* amax_out, void* stream) {
+                   int64_t K, const void* bias, const void* residual, int64_t ldr,
+                   const void* gate, const int32_t* gate_idx, int act, void* D, int64_t ldd,
+                   float* amax_out, void* stream) {
   if (M < 0 || N <= 0 || K <= 0) return H3B_ERR_INVALID_ARG;
+  if (gate_idx && !gate) return H3B_ERR_INVALID_ARG;
   if (gsb_seg < 0 || (gsb_seg && (gsb_seg % 128 || N % gsb_seg))) return H3B_ERR_INVALID_ARG;
   if (K % gemm::KB_ELEMS || N % 128 || a_rows % 128 || a_rows < M) return H3B_ERR_INVALID_ARG;
   if (ldd < N || ldd % 8) return H3B_ERR_INVALID_ARG;
@@ -271,17 +227,11 @@ int h3b_nvfp4_gemm(const void* A, const void* sfA, const float* gsA, int64_t M, 
   if (M == 0) return H3B_OK;
   if (!A || !sfA || !B || !sfB || !D) return H3B_ERR_INVALID_ARG;
   if (!aligned16(A) || !aligned16(B) || !aligned16(sfA) || !aligned16(sfB) || !aligned16(D) ||
-      (bias && !aligned16(bias)) || (residual && !aligned16(residual)))
+      (bias && !aligned16(bias)) || (residual && !aligned16(residual)) ||
+      (gate && !aligned16(gate)))
     return H3B_ERR_ALIGNMENT;
   int st0 = check_sm100();
   if (st0 != H3B_OK) return st0;
-
-  static const bool use_v1 = [] {
-    const char* e = getenv("H3B_GEMM_V1");
-    return e != nullptr && e[0] == '1';
-  }();
-  if (use_v1) return gemm_v1_launch(A, sfA, gsA, M, a_rows, B, sfB, gsB, gsb_seg, N, K, bias,
-                                    residual, ldr, act, D, ldd, amax_out, stream);
 
   static std::once_flag attr_once;
   static cudaError_t attr_err = cudaSuccess;
@@ -309,6 +259,8 @@ int h3b_nvfp4_gemm(const void* A, const void* sfA, const float* gsA, int64_t M, 
   args.gs_b = gsB;
   args.bias = static_cast<const __nv_bfloat16*>(bias);
   args.residual = static_cast<const __nv_bfloat16*>(residual);
+  args.gate = static_cast<const __nv_bfloat16*>(gate);
+  args.gate_idx = gate_idx;
   args.amax_out = amax_out;
   args.ldr = residual ? ldr : 0;
   args.M = (int)M;

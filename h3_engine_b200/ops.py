@@ -120,6 +120,7 @@ def gemm(qa: torch.Tensor, sfa: torch.Tensor, gsa: torch.Tensor | None, M: int,
          qb: torch.Tensor, sfb: torch.Tensor, gsb: torch.Tensor | None, N: int, K: int, *,
          gsb_seg: int = 0, bias: torch.Tensor | None = None,
          residual: torch.Tensor | None = None, act: int = ACT_NONE,
+         gate: torch.Tensor | None = None, gate_idx: torch.Tensor | None = None,
          out: torch.Tensor | None = None, amax_out: torch.Tensor | None = None) -> torch.Tensor:
     """``out[M, N] = epilogue(gsa*gsb * deq(qa) @ deq(qb)^T)`` in bf16.
 
@@ -138,9 +139,15 @@ def gemm(qa: torch.Tensor, sfa: torch.Tensor, gsa: torch.Tensor | None, M: int,
     if residual is not None and (residual.dtype != torch.bfloat16 or residual.stride(-1) != 1):
         raise ValueError("residual must be bf16 with a contiguous last dim")
     ldr = residual.stride(0) if residual is not None else 0
+    if gate is not None and (gate.dtype != torch.bfloat16 or gate.shape[-1] != N
+                             or not gate.is_contiguous()):
+        raise ValueError("gate must be a contiguous bf16 [rows, N] table")
+    if gate_idx is not None and gate_idx.dtype != torch.int32:
+        gate_idx = gate_idx.to(torch.int32)
     st = _lib.lib().h3b_nvfp4_gemm(_p(qa), _p(sfa), _p(gsa), M, a_rows, _p(qb), _p(sfb),
-                                   _p(gsb), gsb_seg, N, K, _p(bias), _p(residual), ldr, act,
-                                   _p(out), out.stride(0), _p(amax_out), _stream(dev))
+                                   _p(gsb), gsb_seg, N, K, _p(bias), _p(residual), ldr,
+                                   _p(gate), _p(gate_idx), act, _p(out), out.stride(0),
+                                   _p(amax_out), _stream(dev))
     _lib.check(st, "h3b_nvfp4_gemm")
     return out
 

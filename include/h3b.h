@@ -99,13 +99,17 @@ H3B_API int h3b_nvfp4_dequantize(const void* q, const void* sf, int sf_layout, i
  *   sfB  swizzled e4m3 scales of B
  *   K    % 256 == 0
  *   epilogue, in order: v = acc*alpha; v += bias[n] (bf16, optional);
- *   v = act(v); v += residual[m, n] (bf16, row stride ldr, optional);
+ *   v = act(v); v *= gate[gate_idx[m], n] (bf16 [rows, N], optional; NULL
+ *   gate_idx means row 0 -- the adaLN-zero gate of gate_residual,
+ *   h3_inference/kernels/elementwise_norm_rope.py:150-163);
+ *   v += residual[m, n] (bf16, row stride ldr, optional);
  *   D = bf16(v); amax_out (optional) is atomically max-reduced with |D|
  *   (the caller zeroes it first).                                            */
 H3B_API int h3b_nvfp4_gemm(const void* A, const void* sfA, const float* gsA, int64_t M, int64_t a_rows,
                    const void* B, const void* sfB, const float* gsB, int64_t gsb_seg, int64_t N,
-                   int64_t K, const void* bias, const void* residual, int64_t ldr, int act,
-                   void* D, int64_t ldd, float* amax_out, void* stream);
+                   int64_t K, const void* bias, const void* residual, int64_t ldr,
+                   const void* gate, const int32_t* gate_idx, int act, void* D, int64_t ldd,
+                   float* amax_out, void* stream);
 
 /* ------------------------------------------------------------------ RMSNorm -> NVFP4
  * The norm that feeds the QKV and FFN-up GEMMs, fused with the activation

@@ -52,11 +52,11 @@ def test_host_validation_rejects_bad_shapes_without_gpu():
                                   1, 128, None) == 2
     # GEMM: K % 256, N % 128, a_rows % 128, unknown activation, bad gsb_seg
     g = lib.h3b_nvfp4_gemm
-    assert g(p, p, None, 128, 128, p, p, None, 0, 256, 128, None, None, 0, 0, p, 256, None, None) == 1
-    assert g(p, p, None, 128, 128, p, p, None, 0, 200, 256, None, None, 0, 0, p, 200, None, None) == 1
-    assert g(p, p, None, 100, 100, p, p, None, 0, 256, 256, None, None, 0, 0, p, 256, None, None) == 1
-    assert g(p, p, None, 128, 128, p, p, None, 0, 256, 256, None, None, 0, 9, p, 256, None, None) == 1
-    assert g(p, p, None, 128, 128, p, p, None, 96, 256, 256, None, None, 0, 0, p, 256, None, None) == 1
+    assert g(p, p, None, 128, 128, p, p, None, 0, 256, 128, None, None, 0, None, None, 0, p, 256, None, None) == 1
+    assert g(p, p, None, 128, 128, p, p, None, 0, 200, 256, None, None, 0, None, None, 0, p, 200, None, None) == 1
+    assert g(p, p, None, 100, 100, p, p, None, 0, 256, 256, None, None, 0, None, None, 0, p, 256, None, None) == 1
+    assert g(p, p, None, 128, 128, p, p, None, 0, 256, 256, None, None, 0, None, None, 9, p, 256, None, None) == 1
+    assert g(p, p, None, 128, 128, p, p, None, 96, 256, 256, None, None, 0, None, None, 0, p, 256, None, None) == 1
     # M == 0 is a no-op that succeeds without touching memory
-    assert g(p, p, None, 0, 128, p, p, None, 0, 256, 256, None, None, 0, 0, p, 256, None, None) == 0
+    assert g(p, p, None, 0, 128, p, p, None, 0, 256, 256, None, None, 0, None, None, 0, p, 256, None, None) == 0
     assert lib.h3b_nvfp4_dequantize(p, p, 1, 100, None, 4, 64, p, None) == 1
