@@ -1,19 +1,31 @@
-"""DiT sub-blocks on the NVFP4 kernels.
+"""DiT sub-blocks on the sm_100a kernels.
 
-``FFNBlock`` is the feed-forward half of a DiT block in the GELU/bias
-configuration: RMSNorm (optionally adaLN-modulated) -> NVFP4 up-projection
+``FFNBlock`` -- the feed-forward half of a DiT block (GELU/bias
+configuration): RMSNorm (optionally adaLN-modulated) -> NVFP4 up-projection
 (+b1, GELU-tanh, |u| max in the epilogue) -> NVFP4 re-quantization of u ->
-NVFP4 down-projection (+b2) + residual.  It is what the reference reaches
-through ``norm_modulate`` + ``ffn`` + ``gate_residual``
+NVFP4 down-projection (+b2, optional adaLN gate) + residual.  The reference
+reaches this through ``norm_modulate`` + ``ffn`` + ``gate_residual``
 (h3_inference/transformer/model.py:200-207,
-h3_inference/kernels/ffn_qkvo_gemms.py:45-54) with the GEMMs on
-``torch._scaled_mm`` and the elementwise work on torch.compile.
+h3_inference/kernels/ffn_qkvo_gemms.py:45-54).
 
-Launches per call: RMSNorm stats, RMSNorm->NVFP4, GEMM-up, quantize,
-GEMM-down (5 kernels) plus one 4-byte memset.  All intermediates live in a
-per-(T, device) workspace that is allocated once.
+``AttnBlock`` -- the attention half: RMSNorm (+modulation) -> NVFP4 QKV
+projection (one GEMM; q/k/v weights keep their own global scales) -> per-head
+qk RMSNorm + 3D RoPE in place -> packed varlen attention -> NVFP4
+quantization of the attention output -> NVFP4 out-projection (+gate) +
+residual (h3_inference/transformer/model.py:81-106,191-198).  With a
+``SequenceShard`` the block runs on this rank's token rows: the projection
+writes Q locally and K|V straight into this rank's rows of the full-sequence
+K|V buffer, one in-place NCCL all-gather completes it, and attention reads
+local queries against all keys.
+
+``DiTBlock`` -- attention then FFN with the six adaLN-zero tables (shift /
+scale / gate per half), gathered per token by ``mod_idx``.
+
+All intermediates live in per-(rows, device) workspaces allocated once.
 """
 from __future__ import annotations
+
+from dataclasses import dataclass
 
 import torch
 
@@ -21,7 +33,31 @@ from . import ops
 from .nvfp4 import NVFP4Weight
 
 
-class FFNBlock:
+class _GemmTimer:
+    """When ``gemm_events`` is a list, (start, end) CUDA events are appended
+    around every GEMM launch on the current stream."""
+
+    gemm_events: list | None = None
+
+    def _event(self, start=None):
+        if self.gemm_events is None:
+            return None
+        e = torch.cuda.Event(enable_timing=True)
+        e.record()
+        if start is not None:
+            self.gemm_events.append((start, e))
+        return e
+
+
+def _buf(ws: dict, name: str, shape, dtype, dev) -> torch.Tensor:
+    t = ws.get(name)
+    if t is None or t.shape != torch.Size(shape) or t.dtype != dtype:
+        t = torch.empty(shape, dtype=dtype, device=dev)
+        ws[name] = t
+    return t
+
+
+class FFNBlock(_GemmTimer):
     def __init__(self, w1: torch.Tensor, b1: torch.Tensor | None, w2: torch.Tensor,
                  b2: torch.Tensor | None, gamma: torch.Tensor, eps: float = 1e-6):
         self.w1 = NVFP4Weight(w1)
@@ -33,9 +69,7 @@ class FFNBlock:
         self.hidden = self.w1.in_features
         self.ffn_dim = self.w1.out_features
         self._ws: dict[tuple, dict] = {}
-        # When a list, (start, end) CUDA events are appended around every GEMM
-        # launch on the current stream (used to time the dominant kernel).
-        self.gemm_events: list | None = None
+        self.gemm_events = None
 
     def flops(self, tokens: int) -> int:
         return 2 * tokens * self.hidden * self.ffn_dim * 2
@@ -59,32 +93,158 @@ class FFNBlock:
 
     def __call__(self, x: torch.Tensor, out: torch.Tensor | None = None, *,
                  shift: torch.Tensor | None = None, scale: torch.Tensor | None = None,
-                 mod_idx: torch.Tensor | None = None) -> torch.Tensor:
+                 gate: torch.Tensor | None = None, mod_idx: torch.Tensor | None = None,
+                 shard: "SequenceShard | None" = None) -> torch.Tensor:
         shape = x.shape
         x2 = x.reshape(-1, shape[-1])
         T = x2.shape[0]
         ws = self._workspace(T, x.device)
+        hook = None if shard is None else shard.reduce_max
         qh, sfh, gsh = ops.rmsnorm_quantize(x2, self.gamma, self.eps, shift=shift, scale=scale,
-                                            mod_idx=mod_idx, ws=ws["norm"])
+                                            mod_idx=mod_idx, ws=ws["norm"], amax_hook=hook)
         ws["amax_u"].zero_()
         ev = self._event()
         u = ops.gemm(qh, sfh, gsh, T, self.w1.qdata, self.w1.scale_u8, self.w1.global_scale,
                      self.ffn_dim, self.hidden, bias=self.b1, act=ops.ACT_GELU_TANH,
                      out=ws["u"], amax_out=ws["amax_u"])
         self._event(ev)
+        if hook is not None:
+            hook(ws["amax_u"])
         qu, sfu, gsu = ops.quantize(u, mpad=qh.shape[0], amax_t=ws["amax_u"], q_out=ws["qu"],
                                     sf_out=ws["sfu"], gs_out=ws["gsu"])
         ev = self._event()
         y = ops.gemm(qu, sfu, gsu, T, self.w2.qdata, self.w2.scale_u8, self.w2.global_scale,
-                     self.hidden, self.ffn_dim, bias=self.b2, residual=x2, out=out)
+                     self.hidden, self.ffn_dim, bias=self.b2, residual=x2, gate=gate,
+                     gate_idx=mod_idx if gate is not None else None, out=out)
         self._event(ev)
         return y.reshape(shape)
 
-    def _event(self, start=None):
-        if self.gemm_events is None:
-            return None
-        e = torch.cuda.Event(enable_timing=True)
-        e.record()
-        if start is not None:
-            self.gemm_events.append((start, e))
-        return e
+
+@dataclass
+class SequenceShard:
+    """This rank's slice ``[row0, row0 + rows)`` of a token-sharded sequence of
+    ``total`` rows, and its collectives:
+
+    * ``all_gather(full, local)``: complete the ``[total, C]`` K|V buffer whose
+      rows ``[row0, row0 + rows)`` (``local``) this rank wrote;
+    * ``reduce_max(t)``: in-place max over the shards of a 1-element fp32
+      amax, so every NVFP4 quantization uses the global scale of the whole
+      sequence (the sharded run then matches the unsharded one).
+    """
+
+    row0: int
+    rows: int
+    total: int
+    all_gather: object
+    reduce_max: object = None
+
+
+class AttnBlock(_GemmTimer):
+    def __init__(self, wq: torch.Tensor, wk: torch.Tensor, wv: torch.Tensor, wo: torch.Tensor,
+                 gamma: torch.Tensor, norm_q: torch.Tensor | None, norm_k: torch.Tensor | None,
+                 heads: int, eps: float = 1e-6, qk_eps: float = 1e-6,
+                 bo: torch.Tensor | None = None):
+        ws = [NVFP4Weight(w) for w in (wq, wk, wv)]
+        self.heads = heads
+        self.inner = ws[0].out_features
+        self.head_dim = self.inner // heads
+        self.hidden = ws[0].in_features
+        # q|k|v packed weights concatenated along N, one global scale each
+        self.w_qkv = torch.cat([w.qdata for w in ws]).contiguous()
+        self.sf_qkv = torch.cat([w.scale_u8 for w in ws]).contiguous()
+        self.gs_qkv = torch.cat([w.global_scale for w in ws]).contiguous()
+        self.wo = NVFP4Weight(wo)
+        self.bo = None if bo is None else bo.to(torch.bfloat16).contiguous()
+        self.gamma = gamma.to(torch.bfloat16).contiguous()
+        self.norm_q = None if norm_q is None else norm_q.to(torch.bfloat16).contiguous()
+        self.norm_k = None if norm_k is None else norm_k.to(torch.bfloat16).contiguous()
+        self.eps, self.qk_eps = float(eps), float(qk_eps)
+        self._ws: dict[tuple, dict] = {}
+        self.gemm_events = None
+
+    def flops(self, tokens: int, cu_seqlens) -> dict:
+        hd, d = self.inner, self.hidden
+        cu = list(cu_seqlens)
+        attn = sum(4 * hd * (b - a) ** 2 for a, b in zip(cu[:-1], cu[1:]))
+        return {"nvfp4": 2 * tokens * d * 3 * hd + 2 * tokens * hd * d, "attention": attn}
+
+    def _sf_rows(self, r0: int, r1: int) -> torch.Tensor:
+        per_row = self.hidden // 16           # scale bytes per weight row (blocked layout)
+        return self.sf_qkv[r0 * per_row:r1 * per_row]
+
+    def __call__(self, x: torch.Tensor, rope: tuple[torch.Tensor, torch.Tensor] | None,
+                 cu_seqlens, out: torch.Tensor | None = None, *,
+                 shift: torch.Tensor | None = None, scale: torch.Tensor | None = None,
+                 gate: torch.Tensor | None = None, mod_idx: torch.Tensor | None = None,
+                 shard: SequenceShard | None = None) -> torch.Tensor:
+        shape = x.shape
+        x2 = x.reshape(-1, shape[-1])
+        T = x2.shape[0]
+        HD, H, D = self.inner, self.heads, self.head_dim
+        dev = x.device
+        ws = self._ws.setdefault((T, dev, shard is not None), {"norm": {}})
+        cos, sin = rope if rope is not None else (None, None)
+        hook = None if shard is None else shard.reduce_max
+        qh, sfh, gsh = ops.rmsnorm_quantize(x2, self.gamma, self.eps, shift=shift, scale=scale,
+                                            mod_idx=mod_idx, ws=ws["norm"], amax_hook=hook)
+        if shard is None:
+            qkv = _buf(ws, "qkv", (T, 3 * HD), torch.bfloat16, dev)
+            ev = self._event()
+            ops.gemm(qh, sfh, gsh, T, self.w_qkv, self.sf_qkv, self.gs_qkv, 3 * HD, self.hidden,
+                     gsb_seg=HD, out=qkv)
+            self._event(ev)
+            ops.qk_norm_rope(qkv, H, D, q_off=0, k_off=HD, wq=self.norm_q, wk=self.norm_k,
+                             eps=self.qk_eps, cos=cos, sin=sin)
+            o = ops.attention_varlen(qkv, H, D, cu_seqlens, q_off=0, k_off=HD, v_off=2 * HD,
+                                     out=_buf(ws, "o", (T, HD), torch.bfloat16, dev))
+        else:
+            if shard.rows != T:
+                raise ValueError("shard rows do not match the local activation")
+            q = _buf(ws, "q", (T, HD), torch.bfloat16, dev)
+            kv = _buf(ws, "kv", (shard.total, 2 * HD), torch.bfloat16, dev)
+            kv_local = kv[shard.row0:shard.row0 + T]
+            ev = self._event()
+            ops.gemm(qh, sfh, gsh, T, self.w_qkv[:HD], self._sf_rows(0, HD), self.gs_qkv[:1], HD,
+                     self.hidden, out=q)
+            ops.gemm(qh, sfh, gsh, T, self.w_qkv[HD:], self._sf_rows(HD, 3 * HD),
+                     self.gs_qkv[1:], 2 * HD, self.hidden, gsb_seg=HD, out=kv_local)
+            self._event(ev)
+            ops.qk_norm_rope(q, H, D, q_off=0, k_off=0, wq=self.norm_q, wk=self.norm_k,
+                             eps=self.qk_eps, cos=cos, sin=sin, k_buf=kv_local)
+            shard.all_gather(kv, kv_local)
+            o = ops.attention_varlen(q, H, D, cu_seqlens, q_off=0, k_off=0, v_off=HD, kv=kv,
+                                     q_row0=shard.row0,
+                                     out=_buf(ws, "o", (T, HD), torch.bfloat16, dev))
+        mp = qh.shape[0]
+        amax_o = ops.amax(o, out=_buf(ws, "amax_o", (1,), torch.float32, dev))
+        if hook is not None:
+            hook(amax_o)
+        qo, sfo, gso = ops.quantize(o, mpad=mp, amax_t=amax_o,
+                                    q_out=_buf(ws, "qo", (mp, HD // 2), torch.uint8, dev),
+                                    sf_out=_buf(ws, "sfo", (mp * (HD // 16),), torch.uint8, dev),
+                                    gs_out=_buf(ws, "gso", (1,), torch.float32, dev))
+        ev = self._event()
+        y = ops.gemm(qo, sfo, gso, T, self.wo.qdata, self.wo.scale_u8, self.wo.global_scale,
+                     self.hidden, HD, bias=self.bo, residual=x2, gate=gate,
+                     gate_idx=mod_idx if gate is not None else None, out=out)
+        self._event(ev)
+        return y.reshape(shape)
+
+
+class DiTBlock:
+    """Attention half then FFN half, each ``x + gate * f(modulate(norm(x)))``
+    (h3_inference/transformer/model.py:176-209)."""
+
+    def __init__(self, attn: AttnBlock, ffn: FFNBlock):
+        self.attn, self.ffn = attn, ffn
+
+    def __call__(self, x: torch.Tensor, rope, cu_seqlens, mod: tuple[torch.Tensor, ...] | None,
+                 mod_idx: torch.Tensor | None = None, out: torch.Tensor | None = None,
+                 shard: SequenceShard | None = None) -> torch.Tensor:
+        if mod is None:
+            sa = ca = ga = sm = cm = gm = None
+        else:
+            sa, ca, ga, sm, cm, gm = mod
+        h = self.attn(x, rope, cu_seqlens, shift=sa, scale=ca, gate=ga, mod_idx=mod_idx,
+                      shard=shard)
+        return self.ffn(h, out=out, shift=sm, scale=cm, gate=gm, mod_idx=mod_idx, shard=shard)

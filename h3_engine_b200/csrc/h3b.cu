@@ -336,9 +336,10 @@ int h3b_rmsnorm_quantize(const void* x, int64_t M, int64_t K, int64_t ldx, const
 }
 
 // ------------------------------------------------------------------ qk-norm + RoPE
-int h3b_qk_norm_rope(void* qkv, int64_t T, int64_t row_stride, int64_t q_off, int64_t k_off,
-                     int H, int D, const void* wq, const void* wk, float eps, const float* cos,
-                     const float* sin, int R, int64_t cs_stride, void* stream) {
+int h3b_qk_norm_rope(void* q, int64_t q_stride, int64_t q_off, void* k, int64_t k_stride,
+                     int64_t k_off, int64_t T, int H, int D, const void* wq, const void* wk,
+                     float eps, const float* cos, const float* sin, int R, int64_t cs_stride,
+                     void* stream) {
   if (T < 0 || H <= 0 || (D != 64 && D != 128)) return H3B_ERR_INVALID_ARG;
   const int epl = D / 32;
   if (cos != nullptr) {
@@ -346,17 +347,19 @@ int h3b_qk_norm_rope(void* qkv, int64_t T, int64_t row_stride, int64_t q_off, in
   } else {
     R = 0;
   }
-  if (q_off < 0 || k_off < 0 || row_stride < (int64_t)H * D ||
-      q_off + (int64_t)H * D > row_stride || k_off + (int64_t)H * D > row_stride)
+  const int64_t hd = (int64_t)H * D;
+  if (q_off < 0 || k_off < 0 || q_off + hd > q_stride || k_off + hd > k_stride)
     return H3B_ERR_INVALID_ARG;
-  if ((row_stride | q_off | k_off) % 8) return H3B_ERR_ALIGNMENT;
+  if ((q_stride | k_stride | q_off | k_off) % 8) return H3B_ERR_ALIGNMENT;
   if (T == 0) return H3B_OK;
-  if (!qkv) return H3B_ERR_INVALID_ARG;
-  if (!aligned16(qkv)) return H3B_ERR_ALIGNMENT;
+  if (!q || !k) return H3B_ERR_INVALID_ARG;
+  if (!aligned16(q) || !aligned16(k)) return H3B_ERR_ALIGNMENT;
   RopeArgs a;
-  a.qkv = static_cast<__nv_bfloat16*>(qkv);
+  a.q = static_cast<__nv_bfloat16*>(q);
+  a.k = static_cast<__nv_bfloat16*>(k);
   a.T = T;
-  a.row_stride = row_stride;
+  a.q_stride = q_stride;
+  a.k_stride = k_stride;
   a.q_off = q_off;
   a.k_off = k_off;
   a.H = H;

@@ -1,5 +1,5 @@
-// Per-head RMSNorm + rotate-half RoPE on q and k, in place in the packed QKV
-// activation (HBM-bound).
+// Per-head RMSNorm + rotate-half RoPE on q and k, in place in the projected
+// query / key activations (HBM-bound).
 //
 // Replaces qk_norm + apply_rotary_emb / norm_rope
 // (h3_inference/kernels/elementwise_norm_rope.py:19-40,104-148) applied to the
@@ -20,9 +20,10 @@
 namespace h3b {
 
 struct RopeArgs {
-  __nv_bfloat16* qkv;      // [T, row_stride]
-  long long T, row_stride;
-  long long q_off, k_off;  // element offsets of the q and k head blocks in a row
+  __nv_bfloat16* q;        // [T, q_stride], q heads at column q_off + h*D
+  __nv_bfloat16* k;        // [T, k_stride], k heads at column k_off + h*D
+  long long T, q_stride, k_stride;
+  long long q_off, k_off;
   int H;                   // heads per block
   int R;                   // rotary dims (even, <= D)
   const __nv_bfloat16* wq; // [D] or null
@@ -51,8 +52,8 @@ __global__ void __launch_bounds__(kRopeWarps * 32) k_qk_norm_rope(const RopeArgs
     const int v = (int)(w - t * 2 * a.H);
     const bool is_k = v >= a.H;
     const int h = is_k ? v - a.H : v;
-    __nv_bfloat16* p = a.qkv + t * a.row_stride + (is_k ? a.k_off : a.q_off) + (long long)h * D +
-                       lane * EPL;
+    __nv_bfloat16* p = (is_k ? a.k + t * a.k_stride + a.k_off : a.q + t * a.q_stride + a.q_off) +
+                       (long long)h * D + lane * EPL;
     float x[EPL];
     if (EPL == 4) {
       const uint2 r = *reinterpret_cast<const uint2*>(p);

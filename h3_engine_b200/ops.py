@@ -155,10 +155,12 @@ def gemm(qa: torch.Tensor, sfa: torch.Tensor, gsa: torch.Tensor | None, M: int,
 def rmsnorm_quantize(x: torch.Tensor, gamma: torch.Tensor, eps: float, *,
                      shift: torch.Tensor | None = None, scale: torch.Tensor | None = None,
                      mod_idx: torch.Tensor | None = None, mpad: int | None = None,
-                     return_y: bool = False, ws: dict | None = None):
+                     return_y: bool = False, ws: dict | None = None, amax_hook=None):
     """Fused RMSNorm(+modulation) -> NVFP4.  Returns (q, sf_swizzled, gs[, y]).
 
     ``ws`` optionally carries preallocated buffers (keys rstd, amax, q, sf, gs, y).
+    ``amax_hook(amax)`` runs between the two passes (e.g. a max all-reduce so
+    that token shards quantize with the global scale of the whole tensor).
     """
     dev = _need_cuda(x, gamma, shift, scale, mod_idx)
     x2 = x.reshape(-1, x.shape[-1]) if x.dim() != 2 else x
@@ -188,6 +190,8 @@ def rmsnorm_quantize(x: torch.Tensor, gamma: torch.Tensor, eps: float, *,
     _lib.check(lib.h3b_rmsnorm_stats(_p(x2), M, K, x2.stride(0), _p(gamma), float(eps), _p(shift),
                                      _p(scale), _p(mod_idx), _p(rstd), _p(am), s),
                "h3b_rmsnorm_stats")
+    if amax_hook is not None:
+        amax_hook(am)
     _lib.check(lib.h3b_rmsnorm_quantize(_p(x2), M, K, x2.stride(0), _p(gamma), _p(shift), _p(scale),
                                         _p(mod_idx), _p(rstd), _p(am), _p(gs), _p(q), _p(sf), Mp,
                                         _p(y), s), "h3b_rmsnorm_quantize")
@@ -196,14 +200,20 @@ def rmsnorm_quantize(x: torch.Tensor, gamma: torch.Tensor, eps: float, *,
 
 def qk_norm_rope(qkv: torch.Tensor, heads: int, head_dim: int, *, q_off: int, k_off: int,
                  wq: torch.Tensor | None, wk: torch.Tensor | None, eps: float,
-                 cos: torch.Tensor | None = None, sin: torch.Tensor | None = None) -> torch.Tensor:
-    """In-place per-head RMSNorm + rotate-half RoPE on the q and k blocks of a
-    packed ``[T, row_stride]`` bf16 activation.  ``cos``/``sin``: fp32 ``[T, R]``."""
-    dev = _need_cuda(qkv, wq, wk, cos, sin)
-    if qkv.dtype != torch.bfloat16 or qkv.stride(-1) != 1:
-        raise ValueError("qkv must be bf16 with a contiguous last dim")
+                 cos: torch.Tensor | None = None, sin: torch.Tensor | None = None,
+                 k_buf: torch.Tensor | None = None) -> torch.Tensor:
+    """In-place per-head RMSNorm + rotate-half RoPE on the query heads of
+    ``qkv`` (at ``q_off``) and the key heads of ``k_buf`` (default ``qkv``, at
+    ``k_off``), both bf16 ``[T, stride]``.  ``cos``/``sin``: fp32 ``[T, R]``."""
+    dev = _need_cuda(qkv, wq, wk, cos, sin, k_buf)
     q2 = qkv.reshape(-1, qkv.shape[-1]) if qkv.dim() != 2 else qkv
+    k2 = q2 if k_buf is None else (k_buf.reshape(-1, k_buf.shape[-1]) if k_buf.dim() != 2 else k_buf)
+    for t in (q2, k2):
+        if t.dtype != torch.bfloat16 or t.stride(-1) != 1:
+            raise ValueError("q / k buffers must be bf16 with a contiguous last dim")
     T = q2.shape[0]
+    if k2.shape[0] != T:
+        raise ValueError("q and k buffers must have the same number of rows")
     R, cs = 0, 0
     if cos is not None:
         if cos.dtype != torch.float32 or sin is None or sin.dtype != torch.float32:
@@ -213,9 +223,9 @@ def qk_norm_rope(qkv: torch.Tensor, heads: int, head_dim: int, *, q_off: int, k_
         if cos.stride(-1) != 1 or sin.stride(-1) != 1 or cos.stride(0) != sin.stride(0):
             cos, sin = cos.contiguous(), sin.contiguous()
         R, cs = cos.shape[1], cos.stride(0)
-    st = _lib.lib().h3b_qk_norm_rope(_p(q2), T, q2.stride(0), q_off, k_off, heads, head_dim,
-                                     _p(wq), _p(wk), float(eps), _p(cos), _p(sin), R, cs,
-                                     _stream(dev))
+    st = _lib.lib().h3b_qk_norm_rope(_p(q2), q2.stride(0), q_off, _p(k2), k2.stride(0), k_off, T,
+                                     heads, head_dim, _p(wq), _p(wk), float(eps), _p(cos),
+                                     _p(sin), R, cs, _stream(dev))
     _lib.check(st, "h3b_qk_norm_rope")
     return qkv
 

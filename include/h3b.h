@@ -134,19 +134,20 @@ H3B_API int h3b_rmsnorm_quantize(const void* x, int64_t M, int64_t K, int64_t ld
                                  void* stream);
 
 /* ------------------------------------------------------------------ qk-norm + RoPE
- * In place on the q and k head blocks of a packed QKV activation
- * qkv[T, row_stride] (bf16): head h of q starts at column q_off + h*D, of k
- * at k_off + h*D.  Per head vector: RMSNorm over D with weight wq / wk (NULL:
- * no norm), then rotate-half RoPE over the first R dims with the (T, R) fp32
- * cos/sin tables (row stride cs_stride; NULL cos: no RoPE), dims >= R pass
- * through.  Replaces qk_norm + apply_rotary_emb / norm_rope
+ * In place on the query and key heads of the projected activations (bf16):
+ * query head h of token t at q[t*q_stride + q_off + h*D], key head h at
+ * k[t*k_stride + k_off + h*D] (q and k may be the same packed QKV buffer).
+ * Per head vector: RMSNorm over D with weight wq / wk (NULL: no norm), then
+ * rotate-half RoPE over the first R dims with the (T, R) fp32 cos/sin tables
+ * (row stride cs_stride; NULL cos: no RoPE), dims >= R pass through.
+ * Replaces qk_norm + apply_rotary_emb / norm_rope
  * (h3_inference/kernels/elementwise_norm_rope.py:19-40,104-148).
- * D in {64, 128}; R even, R <= D, (R/2) % (D/32) == 0; row_stride, q_off,
- * k_off multiples of 8.                                                    */
-H3B_API int h3b_qk_norm_rope(void* qkv, int64_t T, int64_t row_stride, int64_t q_off, int64_t k_off,
-                             int H, int D, const void* wq, const void* wk, float eps,
-                             const float* cos, const float* sin, int R, int64_t cs_stride,
-                             void* stream);
+ * D in {64, 128}; R even, R <= D, (R/2) % (D/32) == 0; strides and offsets
+ * multiples of 8.                                                          */
+H3B_API int h3b_qk_norm_rope(void* q, int64_t q_stride, int64_t q_off, void* k, int64_t k_stride,
+                             int64_t k_off, int64_t T, int H, int D, const void* wq,
+                             const void* wk, float eps, const float* cos, const float* sin, int R,
+                             int64_t cs_stride, void* stream);
 
 /* ------------------------------------------------------------------ packed varlen attention
  * out[i, h*D + d] = softmax_j(q_i . k_j * scale) v_j for every local query row

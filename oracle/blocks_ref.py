@@ -122,3 +122,52 @@ def attention(q, k, v, cu_seqlens, scale: float | None = None, rows=None) -> np.
         p /= p.sum(axis=1, keepdims=True)
         out[i] = np.einsum("hj,jhd->hd", p, v[a:b])
     return out
+
+
+def attn_block(x, gamma, eps, wq, wk, wv, wo, norm_q, norm_k, qk_eps, heads, cos, sin,
+               cu_seqlens, bo=None, shift=None, scale=None, gate=None, mod_idx=None):
+    """Attention half of a DiT block: ``x + gate * out_proj(attn(rope(qk_norm(
+    qkv_proj(modulate(norm(x)))))))`` with every projection an NVFP4 linear
+    (``h3_inference/transformer/model.py:81-106,191-198``).  ``w*`` are (q,
+    sf_rowmajor, gs) triples of quantized weights; the projection input is
+    quantized once and shared by q, k, v (``h3_inference/nvfp4.py:295-302``)."""
+    x = R.bf16_round(x)
+    T = x.shape[0]
+    h = rmsnorm(x, gamma, eps, shift, scale, mod_idx)
+    qa, sa, ga = R.quantize(h)
+    outs = []
+    for w in (wq, wk, wv):
+        y = R.gemm_ref(qa, sa, ga, *w, M=T, N=w[0].shape[0])
+        outs.append(R.bf16_round(y.astype(np.float32)))
+    HD = outs[0].shape[1]
+    D = HD // heads
+    q = qk_norm_rope(outs[0].reshape(T, heads, D), norm_q, qk_eps, cos, sin)
+    k = qk_norm_rope(outs[1].reshape(T, heads, D), norm_k, qk_eps, cos, sin)
+    v = outs[2].reshape(T, heads, D)
+    o = R.bf16_round(attention(q, k, v, cu_seqlens).astype(np.float32)).reshape(T, HD)
+    qo, so, go = R.quantize(o)
+    y = R.gemm_ref(qo, so, go, *wo, M=T, N=wo[0].shape[0])
+    if bo is not None:
+        y = y + R.bf16_round(bo).astype(np.float64)[None, :]
+    if gate is not None:
+        idx = np.zeros(T, dtype=np.int64) if mod_idx is None else np.asarray(mod_idx)
+        y = y * R.bf16_round(gate).astype(np.float64)[idx]
+    y = y + x.astype(np.float64)
+    return R.bf16_round(y.astype(np.float32))
+
+
+def ffn_block_mod(x, gamma, eps, w1q, b1, w2q, b2, shift=None, scale=None, gate=None,
+                  mod_idx=None):
+    """FFN half with adaLN modulation and gate."""
+    x = R.bf16_round(x)
+    h = rmsnorm(x, gamma, eps, shift, scale, mod_idx)
+    u, _ = nvfp4_linear_from_bf16(h, *w1q, bias=b1, act="gelu_tanh")
+    qa, sa, ga = R.quantize(u)
+    y = R.gemm_ref(qa, sa, ga, *w2q, M=x.shape[0], N=w2q[0].shape[0])
+    if b2 is not None:
+        y = y + R.bf16_round(b2).astype(np.float64)[None, :]
+    if gate is not None:
+        idx = np.zeros(x.shape[0], dtype=np.int64) if mod_idx is None else np.asarray(mod_idx)
+        y = y * R.bf16_round(gate).astype(np.float64)[idx]
+    y = y + x.astype(np.float64)
+    return R.bf16_round(y.astype(np.float32))
