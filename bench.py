@@ -1,23 +1,33 @@
 """Benchmark of the NVFP4 DiT hot path on B200.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl h3b|reference]
+                    [--workload dit|ffn]
 
-Workload (one step): the DiT FFN sub-block on 32768 tokens x hidden 3072,
-FFN 12288, seed 2: RMSNorm (eps 1e-6) -> NVFP4 GEMM up (+b1, GELU-tanh) ->
-NVFP4 re-quantization -> NVFP4 GEMM down (+b2) -> residual add, bf16 out.
-Synthetic inputs of the configured shapes/distributions (no dataset).
+Default workload ("dit"): one denoising step of the full multimodal DiT --
+48 blocks (hidden 3072, 24 heads x 128, FFN 12288 GELU/bias, adaLN-zero),
+the packed sequence of 32760 video tokens (21 x 30 x 52 grid, 3D RoPE
+44/42/42) + 1024 audio tokens (two attention documents), CFG batch of 2,
+flow-matching Euler step; random-init weights (seed 4), synthetic latent.
+On N GPUs: N = 1 both CFG branches stacked; N >= 2 CFG split and T/(N/2)
+token shards per branch with one NCCL K|V all-gather per block (strong
+scaling: the total work per step is fixed).
 
-value  = whole-job NVFP4 GEMM throughput: N * 4 * T * d * f flops / step time
-         (max over ranks), TFLOP/s; ms_per_step is the sub-block latency.
-e2e    = the same metric through FFNBlock.__call__ with the step's input
-         copied from pinned host memory and the output copied back, every step.
-Multi-GPU: one process per GPU (torchrun), each rank runs its own 32768
-tokens with replicated weights -- token sharding with no collective on the
-data path, so scaling is weak.
---impl reference: the reference's NVFP4 path cannot run on a CPU (the
-quantizer is in the absent maiku package), so the timed CPU implementation
-is the torch-CPU port of the recipe with the reference's own decode
-(oracle/cpu_torch.py) on a bounded token sample, all host threads.
+value       = whole-job TFLOP/s over every FLOP of the step (NVFP4 GEMMs +
+              bf16 attention), step time = max over ranks of CUDA-event time;
+ms_per_step = the denoising step; block_ms = ms_per_step / 48 (one DiT block
+              of the CFG pair); nvfp4_gemm_tflops = GEMM flops / summed GEMM
+              launch times (per GPU).
+e2e         = the same metric through Sampler.step with the step's latent rows
+              copied in from pinned host memory and the new latent copied back.
+
+"ffn": the DiT FFN sub-block on 32768 tokens x 3072 (FFN 12288), one
+independent shard per GPU (weak scaling, no collective).
+
+--impl reference: the reference's NVFP4 path cannot run on a CPU (its
+quantizer is in the absent maiku package), so the timed CPU implementation is
+the torch-CPU port of the recipe with the reference's own decode
+(oracle/cpu_torch.py) on all host threads, on a bounded sample of query rows
+(attention against full-length keys) extrapolated linearly to the workload.
 """
 from __future__ import annotations
 
@@ -36,15 +46,11 @@ sys.path.insert(0, str(ROOT))
 import torch  # noqa: E402
 
 METRIC = "NVFP4 GEMM TFLOP/s/GPU & % FP4 peak; DiT block latency at 1/2/4/8 B200"
-TOKENS, HIDDEN, FFN = 32768, 3072, 12288
-EPS = 1e-6
-SEED = 2
-WORKLOAD = ("DiT FFN sub-block (seed 2): RMSNorm -> NVFP4 GEMM up 3072->12288 (+bias, GELU-tanh) "
-            "-> NVFP4 re-quant -> NVFP4 GEMM down 12288->3072 (+bias) -> residual")
-# Per-launch DRAM traffic of the dominant kernel (the NVFP4 GEMM), from the
-# committed ncu summary profiles/gemm_nvfp4_ffn.md (dram__bytes_read.sum +
-# dram__bytes_write.sum, mean of the up and down projections).  None until captured.
-GEMM_TRAFFIC_BYTES = None
+FFN_TOKENS, HIDDEN, FFN = 32768, 3072, 12288
+# Per-launch DRAM traffic of the dominant kernel from the committed ncu
+# summaries (dram__bytes_read.sum + dram__bytes_write.sum); None until captured
+# for the kernel and workload named in the roofline object.
+TRAFFIC_BYTES: dict[str, float | None] = {"k_fmha": None, "k_gemm_nvfp4": None}
 
 
 def peaks() -> dict:
@@ -67,6 +73,7 @@ class ClockSampler:
     def __init__(self, gpu_index: int):
         self.gpu = gpu_index
         self.proc = None
+        self.lines: list[str] = []
 
     def __enter__(self):
         try:
@@ -79,7 +86,6 @@ class ClockSampler:
         return self
 
     def __exit__(self, *exc):
-        self.lines = []
         if self.proc is not None:
             time.sleep(0.15)
             self.proc.terminate()
@@ -93,7 +99,7 @@ class ClockSampler:
     def summary(self) -> dict:
         sm, smax, reasons = [], None, set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in getattr(self, "lines", []):
+        for ln in self.lines:
             parts = [p.strip() for p in ln.split(",")]
             if len(parts) < 9:
                 continue
@@ -110,63 +116,182 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(sm)}
 
 
-# ----------------------------------------------------------------------------- inputs
-def make_weights(dev):
-    g = torch.Generator(device="cpu").manual_seed(SEED)
-    w1 = (torch.randn(FFN, HIDDEN, generator=g) * 0.02).to(torch.bfloat16)
-    w2 = (torch.randn(HIDDEN, FFN, generator=g) * 0.02).to(torch.bfloat16)
-    b1 = (torch.randn(FFN, generator=g) * 0.01).to(torch.bfloat16)
-    b2 = (torch.randn(HIDDEN, generator=g) * 0.01).to(torch.bfloat16)
-    gamma = (1 + 0.1 * torch.randn(HIDDEN, generator=g)).to(torch.bfloat16)
-    return [t.to(dev) for t in (w1, b1, w2, b2, gamma)]
+# ----------------------------------------------------------------------------- workloads
+class DiTWorkload:
+    name = "dit"
+
+    def __init__(self, dev, world: int, rank: int, steps_in_schedule: int = 8):
+        from h3_engine_b200.dit import DiTConfig, RandomDiT, Sampler
+        from h3_engine_b200.parallel import ParallelLayout
+
+        self.cfg = DiTConfig()
+        self.layout = ParallelLayout.plan(world, rank)
+        self.layout.build_groups()
+        self.model = RandomDiT(self.cfg, dev, seed=4)
+        self.sampler = Sampler(self.model, self.layout, steps=steps_in_schedule)
+        self.x = self.sampler.latent()
+        self.i = 0
+        f = self.cfg.flops_per_eval()
+        self.step_flops = 2 * (f["nvfp4"] + f["attention"])     # CFG pair, whole job
+        rows = self.sampler.rows.stop - self.sampler.rows.start
+        branches = 2 if self.layout.cfg_parallel == 1 else 1
+        T = self.cfg.tokens
+        d, hd, ff = self.cfg.hidden, self.cfg.heads * self.cfg.head_dim, self.cfg.ffn
+        # this rank's GEMM flops per step (block GEMMs of its rows)
+        self.rank_gemm_flops = self.cfg.blocks * branches * rows * (
+            2 * d * 3 * hd + 2 * hd * d + 4 * d * ff)
+        cu = self.cfg.cu_seqlens()
+        doc_of = [(a, b) for a, b in zip(cu[:-1], cu[1:])]
+        r0, r1 = self.sampler.rows.start, self.sampler.rows.stop
+        self.rank_attn_flops = self.cfg.blocks * branches * sum(
+            4 * hd * max(0, min(b, r1) - max(a, r0)) * (b - a) for a, b in doc_of)
+        self.attn_launches_per_step = self.cfg.blocks
+        self.config = {"workload": "multimodal DiT denoising step (CFG pair): 48 blocks x (attention "
+                                   "sub-block + GELU FFN sub-block), adaLN-zero, seed 4",
+                       "tokens": T, "documents": cu, "hidden": d, "heads": self.cfg.heads,
+                       "head_dim": self.cfg.head_dim, "ffn": ff, "cfg_batch": 2,
+                       "parallelism": (f"cfg{self.layout.cfg_parallel} x "
+                                       f"tokens{self.layout.token_parallel}"),
+                       "l2": "working set several GB per step > 126 MB L2 (no flush needed)"}
+
+    def set_timers(self, gemm, attn):
+        for b in self.model.blocks:
+            b.attn.gemm_events, b.ffn.gemm_events = gemm, gemm
+            b.attn.attn_events = attn
+
+    def step(self):
+        self.x = self.sampler.step(self.x, self.i % self.sampler.steps)
+        self.i += 1
+
+    def e2e_setup(self):
+        self.x_h = self.x.cpu().pin_memory()
+        self.y_h = torch.empty_like(self.x_h).pin_memory()
+        self.x_d = torch.empty_like(self.x)
+        return self.x_h.numel() * 2, self.y_h.numel() * 2
+
+    def e2e_step(self):
+        self.x_d.copy_(self.x_h, non_blocking=True)
+        y = self.sampler.step(self.x_d, self.i % self.sampler.steps)
+        self.i += 1
+        self.y_h.copy_(y, non_blocking=True)
 
 
-def make_tokens(rank: int, dev, n: int = TOKENS):
-    g = torch.Generator(device=dev).manual_seed(SEED * 1000 + rank)
-    return torch.randn(n, HIDDEN, generator=g, device=dev).to(torch.bfloat16)
+class FFNWorkload:
+    name = "ffn"
 
+    def __init__(self, dev, world: int, rank: int, tokens: int = FFN_TOKENS):
+        from h3_engine_b200.blocks import FFNBlock
+        g = torch.Generator(device="cpu").manual_seed(2)
+        w1 = (torch.randn(FFN, HIDDEN, generator=g) * 0.02).to(torch.bfloat16).to(dev)
+        w2 = (torch.randn(HIDDEN, FFN, generator=g) * 0.02).to(torch.bfloat16).to(dev)
+        b1 = (torch.randn(FFN, generator=g) * 0.01).to(torch.bfloat16).to(dev)
+        b2 = (torch.randn(HIDDEN, generator=g) * 0.01).to(torch.bfloat16).to(dev)
+        gamma = (1 + 0.1 * torch.randn(HIDDEN, generator=g)).to(torch.bfloat16).to(dev)
+        self.blk = FFNBlock(w1, b1, w2, b2, gamma, 1e-6)
+        gd = torch.Generator(device=dev).manual_seed(2000 + rank)
+        self.x = torch.randn(tokens, HIDDEN, generator=gd, device=dev).to(torch.bfloat16)
+        self.y = torch.empty_like(self.x)
+        self.step_flops = world * 4.0 * tokens * HIDDEN * FFN
+        self.rank_gemm_flops = 4.0 * tokens * HIDDEN * FFN
+        self.rank_attn_flops = 0
+        self.config = {"workload": "DiT FFN sub-block (seed 2): RMSNorm -> NVFP4 GEMM up 3072->12288 "
+                                   "(+bias, GELU-tanh) -> NVFP4 re-quant -> NVFP4 GEMM down (+bias) "
+                                   "-> residual", "tokens_per_gpu": tokens, "hidden": HIDDEN,
+                       "ffn": FFN, "parallelism": f"token-sharded x{world}, weights replicated",
+                       "l2": "working set ~1.3 GB per step > 126 MB L2 (no flush needed)"}
 
-def gemm_flops(tokens: int) -> float:
-    return 4.0 * tokens * HIDDEN * FFN
+    def set_timers(self, gemm, attn):
+        self.blk.gemm_events = gemm
+
+    def step(self):
+        self.blk(self.x, out=self.y)
+
+    def e2e_setup(self):
+        self.x_h = self.x.cpu().pin_memory()
+        self.y_h = torch.empty_like(self.x_h).pin_memory()
+        self.x_d = torch.empty_like(self.x)
+        return self.x_h.numel() * 2, self.y_h.numel() * 2
+
+    def e2e_step(self):
+        self.x_d.copy_(self.x_h, non_blocking=True)
+        self.blk(self.x_d, out=self.y)
+        self.y_h.copy_(self.y, non_blocking=True)
 
 
 # ----------------------------------------------------------------------------- CPU
-def cpu_sample_run(steps: int, warmup: int, sample_tokens: int) -> dict:
-    """Times the torch-CPU port on a bounded token sample; returns TFLOP/s."""
+def cpu_dit_estimate(sample_rows: int) -> dict:
+    """Extrapolated CPU time of the DiT step from a sample of query rows: the
+    attention half (rows x all keys) and the FFN half of one block on
+    ``sample_rows`` rows, scaled to 2 x T rows x 48 blocks."""
+    from h3_engine_b200.dit import DiTConfig
+    from oracle.cpu_torch import AttnRowsCPU, FFNBlockCPU
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    cfg = DiTConfig()
+    T = cfg.tokens
+    attn = AttnRowsCPU(cfg.hidden, cfg.heads, cfg.head_dim, T)
+    g = torch.Generator().manual_seed(4)
+    w = lambda n, k: (torch.randn(n, k, generator=g) * 0.02).to(torch.bfloat16)  # noqa: E731
+    ffn = FFNBlockCPU(w(cfg.ffn, cfg.hidden), torch.zeros(cfg.ffn), w(cfg.hidden, cfg.ffn),
+                      torch.zeros(cfg.hidden), torch.ones(cfg.hidden), cfg.eps)
+    x = torch.randn(sample_rows, cfg.hidden, generator=g).to(torch.bfloat16)
+    pos = torch.randint(0, 50, (sample_rows, 3), generator=g).float()
+    from h3_engine_b200.rope import rope_tables
+    cos, sin = rope_tables(pos, cfg.rope_dims, cfg.theta)
+    h = attn(x, cos, sin)                       # warm
+    t0 = time.perf_counter()
+    h = attn(x, cos, sin)
+    ffn(h)
+    dt = time.perf_counter() - t0
+    step_s = dt * (2 * T / sample_rows) * cfg.blocks
+    f = cfg.flops_per_eval()
+    flops = 2 * (f["nvfp4"] + f["attention"])
+    return {"value": flops / step_s / 1e12, "unit": "TFLOP/s", "cores": torch.get_num_threads(),
+            "kind": "port", "s_per_step": step_s,
+            "sample": (f"{sample_rows} query rows of one block (attention against all {T} keys "
+                       f"+ FFN), {dt:.2f} s, extrapolated linearly to 2 x {T} rows x "
+                       f"{cfg.blocks} blocks")}
+
+
+def cpu_ffn_run(sample_tokens: int, steps: int = 1) -> dict:
     from oracle.cpu_torch import FFNBlockCPU
 
     torch.set_num_threads(os.cpu_count() or 1)
-    w1, b1, w2, b2, gamma = make_weights("cpu")
-    blk = FFNBlockCPU(w1, b1, w2, b2, gamma, EPS)
-    g = torch.Generator().manual_seed(SEED * 1000)
+    g = torch.Generator(device="cpu").manual_seed(2)
+    w1 = (torch.randn(FFN, HIDDEN, generator=g) * 0.02).to(torch.bfloat16)
+    w2 = (torch.randn(HIDDEN, FFN, generator=g) * 0.02).to(torch.bfloat16)
+    blk = FFNBlockCPU(w1, torch.zeros(FFN), w2, torch.zeros(HIDDEN), torch.ones(HIDDEN), 1e-6)
     x = torch.randn(sample_tokens, HIDDEN, generator=g).to(torch.bfloat16)
-    for _ in range(warmup):
-        blk(x)
+    blk(x)
     t0 = time.perf_counter()
     for _ in range(steps):
         blk(x)
-    dt = (time.perf_counter() - t0) / max(steps, 1)
-    return {"value": gemm_flops(sample_tokens) / dt / 1e12, "unit": "TFLOP/s",
+    dt = (time.perf_counter() - t0) / steps
+    return {"value": 4.0 * sample_tokens * HIDDEN * FFN / dt / 1e12, "unit": "TFLOP/s",
             "cores": torch.get_num_threads(), "kind": "port", "s_per_step": dt,
-            "sample": f"{sample_tokens} of {TOKENS} tokens per step (same weights, seed 2)"}
+            "sample": f"{sample_tokens} of {FFN_TOKENS} tokens per step"}
 
 
 def run_reference(args) -> None:
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
-    r = cpu_sample_run(max(args.steps, 1), max(args.warmup, 0), args.cpu_tokens)
+    vals = []
+    for _ in range(max(args.steps, 1)):
+        r = cpu_dit_estimate(args.cpu_rows) if args.workload == "dit" else cpu_ffn_run(args.cpu_rows)
+        vals.append(r)
+    v = statistics.median([r["value"] for r in vals])
+    r = vals[-1]
     line = {
-        "impl": "reference", "metric": METRIC, "value": r["value"], "unit": "TFLOP/s",
+        "impl": "reference", "metric": METRIC, "value": v, "unit": "TFLOP/s",
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": r["s_per_step"] * 1e3, "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "fp32 (NVFP4 operands decoded)", "data": "synthetic",
-        "config": {"workload": WORKLOAD + f" [CPU sample: {args.cpu_tokens} tokens]",
-                   "tokens": args.cpu_tokens, "hidden": HIDDEN, "ffn": FFN},
-        "cpu_baseline": {"value": r["value"], "unit": "TFLOP/s", "cores": r["cores"],
-                         "kind": r["kind"], "sample": r["sample"]},
-        "e2e": {"value": r["value"], "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
-                "d2h_bytes_per_step": 0},
+        "ms_per_step": statistics.median([x["s_per_step"] for x in vals]) * 1e3,
+        "higher_is_better": True, "scaling": "strong" if args.workload == "dit" else "weak",
+        "vs_baseline": None, "dtype": "fp32 (NVFP4 operands decoded)",
+        "data": "synthetic", "config": {"workload": args.workload + " (CPU, extrapolated sample)"},
+        "cpu_baseline": {"value": v, "unit": "TFLOP/s", "cores": r["cores"], "kind": r["kind"],
+                         "sample": r["sample"]},
+        "e2e": {"value": v, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
 
@@ -176,33 +301,23 @@ def run_ours(args) -> None:
     import torch.distributed as dist
 
     from h3_engine_b200 import _lib
-    from h3_engine_b200.blocks import FFNBlock
+    from h3_engine_b200.parallel import init_distributed
 
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
+    world, rank, local = init_distributed()
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
-    if world > 1:
-        from datetime import timedelta
-        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
 
     def barrier():
         if world > 1:
             dist.barrier()
 
-    w1, b1, w2, b2, gamma = make_weights(dev)
-    blk = FFNBlock(w1, b1, w2, b2, gamma, EPS)
-    tokens = args.tokens
-    x = make_tokens(rank, dev, tokens)
-    y = torch.empty_like(x)
-    flops = gemm_flops(tokens)
-
+    wl = DiTWorkload(dev, world, rank) if args.workload == "dit" else FFNWorkload(dev, world, rank)
     for _ in range(args.warmup):
-        blk(x, out=y)
+        wl.step()
     torch.cuda.synchronize()
 
-    blk.gemm_events = []
+    gemm_ev, attn_ev = [], []
+    wl.set_timers(gemm_ev, attn_ev)
     launches0 = _lib.launch_count()
     barrier()
     torch.cuda.synchronize()
@@ -211,83 +326,96 @@ def run_ours(args) -> None:
         e1 = torch.cuda.Event(enable_timing=True)
         e0.record()
         for _ in range(args.steps):
-            blk(x, out=y)
+            wl.step()
         e1.record()
         torch.cuda.synchronize()
     barrier()
     launches = _lib.launch_count() - launches0
+    wl.set_timers(None, None)
     ms = e0.elapsed_time(e1) / args.steps
-    gemm_ms = [a.elapsed_time(b) for a, b in blk.gemm_events]
-    blk.gemm_events = None
+    gemm_ms = sum(a.elapsed_time(b) for a, b in gemm_ev) / args.steps
+    attn_list = [a.elapsed_time(b) for a, b in attn_ev]
+    attn_ms = sum(attn_list) / args.steps
     err = _lib.device_error()
     if err:
         raise RuntimeError(f"device error {err} during the timed region")
 
-    # e2e through the public call: pinned host in -> block -> pinned host out
-    x_h = x.cpu().pin_memory()
-    y_h = torch.empty_like(x_h).pin_memory()
-    x_d = torch.empty_like(x)
+    h2d, d2h = wl.e2e_setup()
     for _ in range(max(1, min(args.warmup, 2))):
-        x_d.copy_(x_h, non_blocking=True)
-        blk(x_d, out=y)
-        y_h.copy_(y, non_blocking=True)
+        wl.e2e_step()
     torch.cuda.synchronize()
     barrier()
     f0 = torch.cuda.Event(enable_timing=True)
     f1 = torch.cuda.Event(enable_timing=True)
     f0.record()
     for _ in range(args.steps):
-        x_d.copy_(x_h, non_blocking=True)
-        blk(x_d, out=y)
-        y_h.copy_(y, non_blocking=True)
+        wl.e2e_step()
     f1.record()
     torch.cuda.synchronize()
     barrier()
     e2e_ms = f0.elapsed_time(f1) / args.steps
 
-    t = torch.tensor([ms, e2e_ms, statistics.mean(gemm_ms)], dtype=torch.float64, device=dev)
+    t = torch.tensor([ms, e2e_ms], dtype=torch.float64, device=dev)
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms, e2e_ms, gemm_avg = [float(v) for v in t.tolist()]
+    ms, e2e_ms = [float(v) for v in t.tolist()]
 
-    library = None
-    cpu = None
+    extras = {}
     if rank == 0 and not args.no_extras:
-        library = library_gemm_reference(dev)
-    if rank == 0 and world == 1 and not args.no_extras:
-        cpu = cpu_sample_run(1, 0, args.cpu_tokens)
+        extras["library_gemm_torch_scaled_mm"] = library_gemm_reference(dev)
+        if world == 1:
+            cpu = (cpu_dit_estimate(args.cpu_rows) if args.workload == "dit"
+                   else cpu_ffn_run(args.cpu_rows))
+            extras["cpu_baseline"] = {k: cpu[k] for k in ("value", "unit", "cores", "kind", "sample")}
 
     if rank == 0:
         pk = peaks()
-        fp4_peak = 4.0 * pk["bf16_sustained"]
-        achieved = (flops / 2) / (gemm_avg * 1e-3) / 1e12
+        gemm_tflops = wl.rank_gemm_flops / (gemm_ms * 1e-3) / 1e12 if gemm_ms else None
+        if attn_list:
+            n_launch = len(attn_list)
+            flops_launch = wl.rank_attn_flops * args.steps / n_launch
+            achieved = flops_launch / (statistics.mean(attn_list) * 1e-3) / 1e12
+            peak = pk["bf16_sustained"]
+            roof = {"bound": "tensor", "kernel": "h3b::attn::k_fmha (bf16)", "achieved": achieved,
+                    "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
+                    "peak_source": f"bf16_tflops_sustained of {pk['source']} MEASURED_PEAKS.json",
+                    "traffic": TRAFFIC_BYTES["k_fmha"], "per_launch_tflop": flops_launch / 1e12,
+                    "launch_ms": statistics.mean(attn_list),
+                    "share_of_step": attn_ms / ms}
+        else:
+            n_launch = len(gemm_ev)
+            flops_launch = wl.rank_gemm_flops * args.steps / max(n_launch, 1)
+            achieved = wl.rank_gemm_flops / (gemm_ms * 1e-3) / 1e12
+            peak = 4.0 * pk["bf16_sustained"]
+            roof = {"bound": "tensor", "kernel": "h3b::gemm::k_gemm_nvfp4", "achieved": achieved,
+                    "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
+                    "peak_source": f"4 x bf16_tflops_sustained of {pk['source']} "
+                                   "MEASURED_PEAKS.json (dense FP4 = 4x bf16 on B200)",
+                    "traffic": TRAFFIC_BYTES["k_gemm_nvfp4"],
+                    "per_launch_tflop": flops_launch / 1e12, "share_of_step": gemm_ms / ms}
         line = {
             "metric": METRIC,
-            "value": world * flops / (ms * 1e-3) / 1e12,
+            "value": wl.step_flops / (ms * 1e-3) / 1e12,
             "unit": "TFLOP/s",
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-            "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "nvfp4 (e2m1 x e4m3/16 x fp32), fp32 accumulate, bf16 out",
-            "data": "synthetic (seeded, shapes/distributions of the FFN sub-block config)",
-            "config": {"workload": WORKLOAD, "tokens_per_gpu": tokens, "hidden": HIDDEN,
-                       "ffn": FFN, "parallelism": f"token-sharded x{world}, weights replicated",
-                       "l2": "working set ~1.3 GB per step > 126 MB L2 (no flush needed)"},
-            "e2e": {"value": world * flops / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s",
-                    "h2d_bytes_per_step": x.numel() * 2, "d2h_bytes_per_step": y.numel() * 2},
-            "roofline": {"bound": "tensor", "kernel": "h3b::gemm::k_gemm_nvfp4",
-                         "achieved": achieved, "peak": fp4_peak, "unit": "TFLOP/s",
-                         "frac": achieved / fp4_peak,
-                         "peak_source": f"4 x bf16_tflops_sustained of {pk['source']} "
-                                        "MEASURED_PEAKS.json (B200 dense FP4 = 4x bf16 rate)",
-                         "traffic": GEMM_TRAFFIC_BYTES,
-                         "per_launch_gflop": flops / 2 / 1e9, "launch_ms": gemm_avg},
+            "ms_per_step": ms, "higher_is_better": True,
+            "scaling": "strong" if wl.name == "dit" else "weak",
+            "vs_baseline": None,
+            "dtype": "nvfp4 GEMMs (e2m1 x e4m3/16 x fp32 scale, fp32 accumulate) + bf16 attention",
+            "data": "synthetic (seeded random-init weights and latent of the configured shapes)",
+            "config": wl.config,
+            "e2e": {"value": wl.step_flops / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s",
+                    "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+            "roofline": roof,
+            "nvfp4_gemm_tflops_per_gpu": gemm_tflops,
+            "nvfp4_gemm_frac_of_fp4_peak": (gemm_tflops / (4.0 * pk["bf16_sustained"])
+                                            if gemm_tflops else None),
             "gpu_launches": int(launches),
             "clocks": clk.summary(),
         }
-        if library is not None:
-            line["library_gemm_torch_scaled_mm"] = library
-        if cpu is not None:
-            line["cpu_baseline"] = {k: cpu[k] for k in ("value", "unit", "cores", "kind", "sample")}
+        if wl.name == "dit":
+            line["block_ms"] = ms / wl.cfg.blocks
+        line.update(extras)
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()
@@ -295,12 +423,13 @@ def run_ours(args) -> None:
 
 
 def library_gemm_reference(dev) -> dict | None:
-    """torch._scaled_mm (cuBLASLt NVFP4, the reference's GEMM call) on the
-    same two GEMM shapes, for context; not part of the timed step."""
+    """torch._scaled_mm (cuBLASLt NVFP4, the reference's GEMM call) on the FFN
+    GEMM shapes, for context; not part of the timed step."""
     try:
         from h3_engine_b200 import ops
         out = {}
-        for name, (M, N, K) in {"up": (TOKENS, FFN, HIDDEN), "down": (TOKENS, HIDDEN, FFN)}.items():
+        for name, (M, N, K) in {"up": (FFN_TOKENS, FFN, HIDDEN),
+                                "down": (FFN_TOKENS, HIDDEN, FFN)}.items():
             a = torch.randn(M, K, device=dev).to(torch.bfloat16)
             b = (torch.randn(N, K, device=dev) * 0.02).to(torch.bfloat16)
             qa, sa, _ = ops.quantize(a, mpad=M, gs=1.0)
@@ -326,13 +455,12 @@ def library_gemm_reference(dev) -> dict | None:
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["h3b", "reference"], default="h3b")
-    ap.add_argument("--tokens", type=int, default=TOKENS,
-                    help="tokens per GPU (default: the configured 32768; smaller for ncu captures)")
-    ap.add_argument("--cpu-tokens", type=int, default=1024,
-                    help="token sample for the CPU baseline")
+    ap.add_argument("--workload", choices=["dit", "ffn"], default="dit")
+    ap.add_argument("--cpu-rows", type=int, default=64,
+                    help="query rows (dit) / tokens (ffn) of the CPU sample")
     ap.add_argument("--no-extras", action="store_true",
                     help="skip the library GEMM comparison and the CPU baseline (profiling runs)")
     args = ap.parse_args()

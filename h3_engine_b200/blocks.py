@@ -34,18 +34,21 @@ from .nvfp4 import NVFP4Weight
 
 
 class _GemmTimer:
-    """When ``gemm_events`` is a list, (start, end) CUDA events are appended
-    around every GEMM launch on the current stream."""
+    """When ``gemm_events`` / ``attn_events`` are lists, (start, end) CUDA
+    events are appended around every GEMM / attention launch on the current
+    stream (how bench.py times the dominant kernels inside a real step)."""
 
     gemm_events: list | None = None
+    attn_events: list | None = None
 
-    def _event(self, start=None):
-        if self.gemm_events is None:
+    def _event(self, start=None, sink=None):
+        sink = self.gemm_events if sink is None else sink
+        if sink is None:
             return None
         e = torch.cuda.Event(enable_timing=True)
         e.record()
         if start is not None:
-            self.gemm_events.append((start, e))
+            sink.append((start, e))
         return e
 
 
@@ -59,7 +62,8 @@ def _buf(ws: dict, name: str, shape, dtype, dev) -> torch.Tensor:
 
 class FFNBlock(_GemmTimer):
     def __init__(self, w1: torch.Tensor, b1: torch.Tensor | None, w2: torch.Tensor,
-                 b2: torch.Tensor | None, gamma: torch.Tensor, eps: float = 1e-6):
+                 b2: torch.Tensor | None, gamma: torch.Tensor, eps: float = 1e-6,
+                 workspace: dict | None = None):
         self.w1 = NVFP4Weight(w1)
         self.w2 = NVFP4Weight(w2)
         self.b1 = None if b1 is None else b1.to(torch.bfloat16).contiguous()
@@ -68,14 +72,15 @@ class FFNBlock(_GemmTimer):
         self.eps = float(eps)
         self.hidden = self.w1.in_features
         self.ffn_dim = self.w1.out_features
-        self._ws: dict[tuple, dict] = {}
+        # blocks that run one after another on one stream may share one pool
+        self._ws: dict[tuple, dict] = {} if workspace is None else workspace
         self.gemm_events = None
 
     def flops(self, tokens: int) -> int:
         return 2 * tokens * self.hidden * self.ffn_dim * 2
 
     def _workspace(self, T: int, dev: torch.device) -> dict:
-        key = (T, dev)
+        key = ("ffn", T, self.hidden, self.ffn_dim, dev)
         ws = self._ws.get(key)
         if ws is None:
             Tp = ops.pad_m(T)
@@ -126,10 +131,12 @@ class SequenceShard:
     ``total`` rows, and its collectives:
 
     * ``all_gather(full, local)``: complete the ``[total, C]`` K|V buffer whose
-      rows ``[row0, row0 + rows)`` (``local``) this rank wrote;
-    * ``reduce_max(t)``: in-place max over the shards of a 1-element fp32
-      amax, so every NVFP4 quantization uses the global scale of the whole
-      sequence (the sharded run then matches the unsharded one).
+      rows ``[row0, row0 + rows)`` (``local``) this rank wrote; None when the
+      sequence is not split (rows == total, e.g. a CFG-split run);
+    * ``reduce_max(t)``: in-place max over every rank holding part of the
+      activation tensor of a 1-element fp32 amax, so every NVFP4 quantization
+      uses the global scale of the whole tensor (the distributed run then
+      computes the same bytes as the single-GPU one).
     """
 
     row0: int
@@ -137,13 +144,20 @@ class SequenceShard:
     total: int
     all_gather: object
     reduce_max: object = None
+    chunk: int = 0        # rows per shard in the gathered buffer (0: ``rows``)
+    parts: int = 0        # shards (0: ceil(total / chunk))
+
+    def buffer_rows(self) -> int:
+        chunk = self.chunk or self.rows
+        parts = self.parts or -(-self.total // chunk)
+        return max(self.total, chunk * parts)
 
 
 class AttnBlock(_GemmTimer):
     def __init__(self, wq: torch.Tensor, wk: torch.Tensor, wv: torch.Tensor, wo: torch.Tensor,
                  gamma: torch.Tensor, norm_q: torch.Tensor | None, norm_k: torch.Tensor | None,
                  heads: int, eps: float = 1e-6, qk_eps: float = 1e-6,
-                 bo: torch.Tensor | None = None):
+                 bo: torch.Tensor | None = None, workspace: dict | None = None):
         ws = [NVFP4Weight(w) for w in (wq, wk, wv)]
         self.heads = heads
         self.inner = ws[0].out_features
@@ -159,7 +173,7 @@ class AttnBlock(_GemmTimer):
         self.norm_q = None if norm_q is None else norm_q.to(torch.bfloat16).contiguous()
         self.norm_k = None if norm_k is None else norm_k.to(torch.bfloat16).contiguous()
         self.eps, self.qk_eps = float(eps), float(qk_eps)
-        self._ws: dict[tuple, dict] = {}
+        self._ws: dict[tuple, dict] = {} if workspace is None else workspace
         self.gemm_events = None
 
     def flops(self, tokens: int, cu_seqlens) -> dict:
@@ -182,12 +196,13 @@ class AttnBlock(_GemmTimer):
         T = x2.shape[0]
         HD, H, D = self.inner, self.heads, self.head_dim
         dev = x.device
-        ws = self._ws.setdefault((T, dev, shard is not None), {"norm": {}})
+        split = shard is not None and shard.all_gather is not None
+        ws = self._ws.setdefault(("attn", T, self.hidden, self.inner, dev, split), {"norm": {}})
         cos, sin = rope if rope is not None else (None, None)
         hook = None if shard is None else shard.reduce_max
         qh, sfh, gsh = ops.rmsnorm_quantize(x2, self.gamma, self.eps, shift=shift, scale=scale,
                                             mod_idx=mod_idx, ws=ws["norm"], amax_hook=hook)
-        if shard is None:
+        if shard is None or shard.all_gather is None:
             qkv = _buf(ws, "qkv", (T, 3 * HD), torch.bfloat16, dev)
             ev = self._event()
             ops.gemm(qh, sfh, gsh, T, self.w_qkv, self.sf_qkv, self.gs_qkv, 3 * HD, self.hidden,
@@ -195,13 +210,15 @@ class AttnBlock(_GemmTimer):
             self._event(ev)
             ops.qk_norm_rope(qkv, H, D, q_off=0, k_off=HD, wq=self.norm_q, wk=self.norm_k,
                              eps=self.qk_eps, cos=cos, sin=sin)
+            ev = self._event(sink=self.attn_events)
             o = ops.attention_varlen(qkv, H, D, cu_seqlens, q_off=0, k_off=HD, v_off=2 * HD,
                                      out=_buf(ws, "o", (T, HD), torch.bfloat16, dev))
+            self._event(ev, sink=self.attn_events)
         else:
             if shard.rows != T:
                 raise ValueError("shard rows do not match the local activation")
             q = _buf(ws, "q", (T, HD), torch.bfloat16, dev)
-            kv = _buf(ws, "kv", (shard.total, 2 * HD), torch.bfloat16, dev)
+            kv = _buf(ws, "kv", (shard.buffer_rows(), 2 * HD), torch.bfloat16, dev)
             kv_local = kv[shard.row0:shard.row0 + T]
             ev = self._event()
             ops.gemm(qh, sfh, gsh, T, self.w_qkv[:HD], self._sf_rows(0, HD), self.gs_qkv[:1], HD,
@@ -212,9 +229,12 @@ class AttnBlock(_GemmTimer):
             ops.qk_norm_rope(q, H, D, q_off=0, k_off=0, wq=self.norm_q, wk=self.norm_k,
                              eps=self.qk_eps, cos=cos, sin=sin, k_buf=kv_local)
             shard.all_gather(kv, kv_local)
-            o = ops.attention_varlen(q, H, D, cu_seqlens, q_off=0, k_off=0, v_off=HD, kv=kv,
+            ev = self._event(sink=self.attn_events)
+            o = ops.attention_varlen(q, H, D, cu_seqlens, q_off=0, k_off=0, v_off=HD,
+                                     kv=kv[:shard.total],
                                      q_row0=shard.row0,
                                      out=_buf(ws, "o", (T, HD), torch.bfloat16, dev))
+            self._event(ev, sink=self.attn_events)
         mp = qh.shape[0]
         amax_o = ops.amax(o, out=_buf(ws, "amax_o", (1,), torch.float32, dev))
         if hook is not None:
@@ -223,6 +243,8 @@ class AttnBlock(_GemmTimer):
                                     q_out=_buf(ws, "qo", (mp, HD // 2), torch.uint8, dev),
                                     sf_out=_buf(ws, "sfo", (mp * (HD // 16),), torch.uint8, dev),
                                     gs_out=_buf(ws, "gso", (1,), torch.float32, dev))
+        if out is None:
+            out = _buf(ws, "y", (T, self.hidden), torch.bfloat16, dev)
         ev = self._event()
         y = ops.gemm(qo, sfo, gso, T, self.wo.qdata, self.wo.scale_u8, self.wo.global_scale,
                      self.hidden, HD, bias=self.bo, residual=x2, gate=gate,

@@ -80,3 +80,54 @@ class FFNBlockCPU:
         cu, su, gu = quantize(u.float(), gs_u)
         y = F.linear(dequantize(cu, su, gu), self.w2, self.b2) + x.float()
         return y.to(torch.bfloat16)
+
+
+def qk_norm_rope(x: torch.Tensor, w: torch.Tensor, eps: float, cos: torch.Tensor,
+                 sin: torch.Tensor) -> torch.Tensor:
+    """[S, H, D] bf16 -> per-head RMSNorm + rotate-half RoPE (reference formula,
+    h3_inference/kernels/elementwise_norm_rope.py:104-122), bf16 out."""
+    xf = x.float()
+    xn = xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + eps) * w.float()
+    r = cos.shape[-1]
+    half = r // 2
+    c = cos.to(torch.bfloat16).float()[:, None, :]
+    s = sin.to(torch.bfloat16).float()[:, None, :]
+    x1, x2 = xn[..., :half], xn[..., half:r]
+    out = torch.cat([x1 * c[..., :half] - x2 * s[..., :half],
+                     x2 * c[..., half:] + x1 * s[..., half:], xn[..., r:]], dim=-1)
+    return out.to(torch.bfloat16)
+
+
+class AttnRowsCPU:
+    """Attention half of a DiT block for a SAMPLE of query rows against keys /
+    values of the full sequence: norm -> NVFP4 (decoded) QKV projection of the
+    sample -> qk-norm + RoPE -> softmax attention over all T keys -> NVFP4
+    out-projection + residual.  The keys / values of the other rows are random
+    stand-ins: the cost per query row is that of the full computation."""
+
+    def __init__(self, d: int, heads: int, head_dim: int, total: int, seed: int = 4):
+        g = torch.Generator().manual_seed(seed)
+        hd = heads * head_dim
+        self.heads, self.head_dim = heads, head_dim
+        w = lambda n, k: (torch.randn(n, k, generator=g) * 0.02).to(torch.bfloat16)  # noqa: E731
+        self.wqkv = [dequantize(*quantize(w(hd, d).float())) for _ in range(3)]
+        self.wo = dequantize(*quantize(w(d, hd).float()))
+        self.gamma = (1 + 0.1 * torch.randn(d, generator=g)).to(torch.bfloat16)
+        self.nq = (1 + 0.1 * torch.randn(head_dim, generator=g)).to(torch.bfloat16)
+        self.nk = (1 + 0.1 * torch.randn(head_dim, generator=g)).to(torch.bfloat16)
+        self.k_all = torch.randn(heads, total, head_dim, generator=g).to(torch.bfloat16).float()
+        self.v_all = torch.randn(heads, total, head_dim, generator=g).to(torch.bfloat16).float()
+
+    def __call__(self, x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor) -> torch.Tensor:
+        S = x.shape[0]
+        h = rmsnorm(x, self.gamma, 1e-6)
+        c, s, g = quantize(h.float())
+        hq = dequantize(c, s, g)
+        q, k, v = (F.linear(hq, w).to(torch.bfloat16).view(S, self.heads, self.head_dim)
+                   for w in self.wqkv)
+        q = qk_norm_rope(q, self.nq, 1e-6, cos, sin)
+        qf = q.float().transpose(0, 1)                                   # [H, S, D]
+        p = torch.softmax(qf @ self.k_all.transpose(1, 2) * self.head_dim ** -0.5, dim=-1)
+        o = (p @ self.v_all).transpose(0, 1).reshape(S, -1).to(torch.bfloat16)
+        c, s, g = quantize(o.float())
+        return (F.linear(dequantize(c, s, g), self.wo) + x.float()).to(torch.bfloat16)

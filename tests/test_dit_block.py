@@ -99,7 +99,7 @@ def test_sharded_attn_block_reproduces_unsharded(cuda):
     cos, sin = (t.to(cuda) for t in rope_tables(positions(T), (44, 42, 42), 1e4))
     blk = build_attn(p, H, cuda)
     full = blk(x, (cos, sin), cu).clone()
-    ws = blk._ws[(T, x.device, False)]
+    ws = blk._ws[("attn", T, d, HD, x.device, False)]
     amax_norm = ws["norm"]["amax"].clone()
     amax_o = ws["amax_o"].clone()
     kv_ref = ws["qkv"][:, HD:].clone()
