@@ -7,20 +7,27 @@
 // packing (cu_seqlens).  A single document reproduces the reference model,
 // which attends over the whole packed sequence.
 //
-// One CTA = one 128-row query tile of one head of one document:
-//   warp 0      TMA producer: Q tile once, then K and V tiles (128 rows x 128)
-//               into two separate 2-stage rings, read straight from the packed
-//               QKV activation (q|k|v blocks of one [T, row_stride] buffer).
-//   warp 1      TMEM allocator + single-thread MMA issuer:
-//                 S_j = Q K_j^T   (tcgen05.mma kind::f16, SS, M=128 N=128 K=16 x8)
-//                 O  += P_j V_j   (TS form: P_j read from tensor memory, V_j
-//                                  MN-major from shared memory)
-//   warps 2-5   softmax + epilogue, one query row per thread: read S_j from
-//               TMEM, online softmax in the exp2 domain, write P_j (bf16) back
-//               into S_j's columns; O is rescaled in TMEM only when a row max
-//               grows by more than 2^8 (the final O / l is exact either way);
-//               at the end O / l -> bf16 -> global.
-// TMEM: three S buffers (cols 0..383, QK_{j+1} overlaps softmax_j) + O (384..511).
+// One CTA = two 128-row query tiles (A, B) of one head of one document; K/V
+// tiles are loaded once for both:
+//   warp 8      TMA producer: Q_A, Q_B once, then K and V tiles (128 rows x 128)
+//               into two separate 2-stage rings, read straight from the q / kv
+//               activations.
+//   warp 9      TMEM allocator + single-thread MMA issuer.  One in-order MMA
+//               stream, staggered so the tensor core works on one tile while
+//               the other tile's softmax runs:
+//                 QK_A(0) QK_B(0) | PV_A(j) QK_A(j+1) PV_B(j) QK_B(j+1) | ...
+//               S = Q K^T: tcgen05.mma kind::f16, SS, M=128 N=128 K=16 x8;
+//               O += P V: TS form, P read from tensor memory, V MN-major.
+//               P_X(j) lives in the columns of S_X; QK_X(j+1) overwrites them
+//               only after PV_X(j), in issue order.
+//   warps 0-3   softmax of tile A, warps 4-7 of tile B (one query row per
+//               thread): the row of S is read from TMEM into registers once,
+//               its max taken, exponentiated (5/8 on the MUFU ex2 unit, 3/8 by
+//               an FMA polynomial), summed and written back as P (bf16); O is
+//               rescaled in TMEM only when a row max grows by more than 2^8
+//               (the final O / l is exact either way); at the end
+//               O / l -> bf16 -> global.
+// TMEM: S_A [0,128), S_B [128,256), O_A [256,384), O_B [384,512).
 // Every wait is bounded (2 s); on expiry the CTA records H3B_ERR_TIMEOUT and
 // unwinds.
 #pragma once
@@ -30,19 +37,28 @@
 namespace h3b {
 namespace attn {
 
-constexpr int BQ = 128;          // query rows per CTA
+constexpr int BQ = 128;          // query rows per tile (two tiles per CTA)
 constexpr int BK = 128;          // key / value rows per step
 constexpr int D = 128;           // head dim
 constexpr int TILE_BYTES = BQ * D * 2;   // 32 KiB (two 64-column, 128B-swizzled boxes)
 constexpr int BOX_BYTES = TILE_BYTES / 2;
-constexpr int Q_OFF = 0;
-constexpr int K_OFF = TILE_BYTES;                  // 2 stages
+constexpr int Q_OFF = 0;                           // Q_A, Q_B
+constexpr int K_OFF = 2 * TILE_BYTES;              // 2 stages
 constexpr int V_OFF = K_OFF + 2 * TILE_BYTES;      // 2 stages
 constexpr int BAR_OFF = V_OFF + 2 * TILE_BYTES;
 constexpr int SMEM_BYTES = BAR_OFF + 256 + 1024;
-constexpr int THREADS = 192;
+constexpr int THREADS = 384;       // three warpgroups: softmax A, softmax B, producer + MMA
+// Register split (setmaxnreg): the kernel launches at kLaunchRegs per thread
+// (three warps per SM sub-partition); the producer/MMA warpgroup gives back
+// down to kCtrlRegs so the two softmax warpgroups can hold a whole 128-key row
+// of S: 128 * kCtrlRegs + 256 * kSoftmaxRegs == THREADS * kLaunchRegs.
+constexpr int kLaunchRegs = 168;
+constexpr int kCtrlRegs = 56;
+constexpr int kSoftmaxRegs = 224;
+static_assert(128 * kCtrlRegs + 256 * kSoftmaxRegs <= THREADS * kLaunchRegs, "register split");
 constexpr uint32_t TMEM_COLS = 512;
-constexpr uint32_t O_COL = 384;
+__host__ __device__ constexpr uint32_t s_col(int t) { return (uint32_t)t * 128u; }
+__host__ __device__ constexpr uint32_t o_col(int t) { return 256u + (uint32_t)t * 128u; }
 constexpr int MAX_DOCS = 64;
 // kind::f16: D fp32 (bit 4), A = B = bf16 (bits 7, 10), N>>3 at 17, M>>4 at 24
 constexpr uint32_t IDESC_QK = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BK >> 3) << 17) |
@@ -66,13 +82,99 @@ struct Args {
   int doc_len[MAX_DOCS];   // keys in the document
   int q_start[MAX_DOCS];   // first local query row of the document (q buffer rows)
   int q_len[MAX_DOCS];     // local queries in the document
-  int item_end[MAX_DOCS];  // cumulative CTA counts (q_tiles * H) per document
+  int item_end[MAX_DOCS];  // cumulative CTA counts (query-tile pairs * H) per document
 };
 
 __device__ __forceinline__ float ex2(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
+}
+
+// Packed two-lane fp32 arithmetic (one instruction for both lanes on sm_100).
+__device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) {
+  float2 d;
+  asm("{\n.reg .b64 a, b, c, d;\nmov.b64 a, {%2, %3};\nmov.b64 b, {%4, %5};\n"
+      "mov.b64 c, {%6, %7};\nfma.rn.f32x2 d, a, b, c;\nmov.b64 {%0, %1}, d;\n}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
+  return d;
+}
+__device__ __forceinline__ float2 add2(float2 a, float2 b) {
+  float2 d;
+  asm("{\n.reg .b64 a, b, d;\nmov.b64 a, {%2, %3};\nmov.b64 b, {%4, %5};\n"
+      "add.rn.f32x2 d, a, b;\nmov.b64 {%0, %1}, d;\n}"
+      : "=f"(d.x), "=f"(d.y) : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return d;
+}
+__device__ __forceinline__ float2 sub2(float2 a, float2 b) {
+  float2 d;
+  asm("{\n.reg .b64 a, b, d;\nmov.b64 a, {%2, %3};\nmov.b64 b, {%4, %5};\n"
+      "sub.rn.f32x2 d, a, b;\nmov.b64 {%0, %1}, d;\n}"
+      : "=f"(d.x), "=f"(d.y) : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return d;
+}
+__device__ __forceinline__ float max3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
+// 2^x for two lanes on the FMA pipe: x = n + f with n = round(x) (adding
+// 1.5 * 2^23 rounds to an integer in the low mantissa bits), f in [-0.5, 0.5];
+// 2^f by a cubic fitted here by relative-error-weighted least squares on
+// Chebyshev nodes (max relative error 1.2e-4, below the bf16 rounding P
+// receives); 2^n added into the exponent field.  x is clamped to >= -120 so the
+// result stays a normal number; callers never pass masked keys here.
+__device__ __forceinline__ float2 ex2_poly2(float2 x) {
+  x.x = fmaxf(x.x, -120.0f);
+  x.y = fmaxf(x.y, -120.0f);
+  const float2 magic = make_float2(12582912.0f, 12582912.0f);
+  const float2 t = add2(x, magic);
+  const float2 f = sub2(x, sub2(t, magic));
+  float2 q = fma2(f, make_float2(0.05459282547235489f, 0.05459282547235489f),
+                  make_float2(0.24221783876419067f, 0.24221783876419067f));
+  q = fma2(f, q, make_float2(0.6933686137199402f, 0.6933686137199402f));
+  q = fma2(f, q, make_float2(1.0f, 1.0f));
+  return make_float2(__int_as_float(__float_as_int(q.x) + (__float_as_int(t.x) << 23)),
+                     __int_as_float(__float_as_int(q.y) + (__float_as_int(t.y) << 23)));
+}
+
+// Key pairs (of each 8) whose exponentials go to the FMA polynomial; the rest
+// use the MUFU ex2 unit (16 results per clock per SM).
+constexpr uint32_t kPolyPairs = 0x52u;   // pairs 1, 4, 6
+
+// P = 2^(S * scale_log2 - m) for one 128-key row held in registers, packed to
+// bf16 pairs and stored over the first 64 columns of the row's S in tensor
+// memory; returns the row sum (two lanes).  MIXED splits the exponentials
+// between MUFU and the polynomial; the partial last tile of a document uses
+// MUFU only, where a masked key (S = -inf) gives exactly 0.
+template <bool MIXED>
+__device__ __forceinline__ float2 softmax_exp_store(uint32_t (&sv)[128], float scale_log2,
+                                                    float m, uint32_t s_addr) {
+  const float2 sc = make_float2(scale_log2, scale_log2);
+  const float2 nm = make_float2(-m, -m);
+  float2 acc0 = make_float2(0.f, 0.f), acc1 = make_float2(0.f, 0.f);
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    uint32_t pk[32];
+#pragma unroll
+    for (int c = 0; c < 32; ++c) {
+      const int k = h * 64 + 2 * c;
+      const float2 x = fma2(make_float2(__uint_as_float(sv[k]), __uint_as_float(sv[k + 1])), sc, nm);
+      float2 e;
+      if (MIXED && ((kPolyPairs >> (c & 7)) & 1u)) {
+        e = ex2_poly2(x);
+      } else {
+        e = make_float2(ex2(x.x), ex2(x.y));
+      }
+      if (c & 1) acc1 = add2(acc1, e);
+      else acc0 = add2(acc0, e);
+      pk[c] = pack_bf16x2(e.x, e.y);
+    }
+    tmem_st_32x32b_x32(s_addr + h * 32, pk);
+  }
+  return add2(acc0, acc1);
 }
 
 __global__ void __launch_bounds__(THREADS, 1) k_fmha(const __grid_constant__ Args p) {
@@ -85,27 +187,27 @@ __global__ void __launch_bounds__(THREADS, 1) k_fmha(const __grid_constant__ Arg
   uint64_t* k_empty = bars + 3;      // 2
   uint64_t* v_full = bars + 5;       // 2
   uint64_t* v_empty = bars + 7;      // 2
-  uint64_t* s_full = bars + 9;       // 3
-  uint64_t* p_full = bars + 12;      // 3
-  uint64_t* pv_done = bars + 15;     // 3
-  uint64_t* drain = bars + 18;       // 1
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 19);
+  uint64_t* s_full = bars + 9;       // 2 (tile A, B)
+  uint64_t* p_full = bars + 11;      // 2
+  uint64_t* pv_done = bars + 13;     // 2
+  uint64_t* drain = bars + 15;       // 1
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
-  // work item -> (document, query tile, head); query tiles vary fastest so
+  // work item -> (document, query-tile pair, head); pairs vary fastest so
   // neighbouring CTAs share K / V of one head in L2
   int doc = 0;
   while (doc + 1 < p.ndocs && (int)blockIdx.x >= p.item_end[doc]) ++doc;
   const int item = (int)blockIdx.x - (doc > 0 ? p.item_end[doc - 1] : 0);
   const int len = p.doc_len[doc];
   const int q_len = p.q_len[doc];
-  const int q_tiles = (q_len + BQ - 1) / BQ;
-  const int head = item / q_tiles;
-  const int qt = item - head * q_tiles;
+  const int pairs = (q_len + 2 * BQ - 1) / (2 * BQ);
+  const int head = item / pairs;
+  const int qp = item - head * pairs;
   const int row0 = p.doc_start[doc];
-  const int q_row = p.q_start[doc] + qt * BQ;   // local row in the q / out buffers
+  const int q_row = p.q_start[doc] + qp * 2 * BQ;   // local row of tile A
   const int n_kv = (len + BK - 1) / BK;
 
   if (threadIdx.x == 0) {
@@ -115,8 +217,6 @@ __global__ void __launch_bounds__(THREADS, 1) k_fmha(const __grid_constant__ Arg
       mbar_init(smem_u32(&k_empty[i]), 1);
       mbar_init(smem_u32(&v_full[i]), 1);
       mbar_init(smem_u32(&v_empty[i]), 1);
-    }
-    for (int i = 0; i < 3; ++i) {
       mbar_init(smem_u32(&s_full[i]), 1);
       mbar_init(smem_u32(&p_full[i]), 4);
       mbar_init(smem_u32(&pv_done[i]), 1);
@@ -125,7 +225,7 @@ __global__ void __launch_bounds__(THREADS, 1) k_fmha(const __grid_constant__ Arg
     *abort_flag = 0;
     fence_mbar_init();
   }
-  if (warp == 1) {
+  if (warp == 9) {
     tmem_alloc(smem_u32(tmem_slot), TMEM_COLS);
     tmem_relinquish();
   }
@@ -141,48 +241,46 @@ __global__ void __launch_bounds__(THREADS, 1) k_fmha(const __grid_constant__ Arg
     }
   };
 
-  if (warp == 0) {
+  // Each warpgroup changes its register limit inside its own branch and leaves
+  // through its own copy of the teardown barrier, so no code runs under two
+  // limits.
+  if (warp >= 8) {
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kCtrlRegs));
+   if (warp == 8) {
     if (lane == 0) {
       prefetch_tmap(&p.tmap_q);
       prefetch_tmap(&p.tmap_kv);
       const int qx = p.q_off + head * D, kx = p.k_off + head * D, vx = p.v_off + head * D;
       uint32_t fb = smem_u32(q_full);
-      mbar_expect_tx(fb, TILE_BYTES);
-      tma_load_2d(smem_u32(smem + Q_OFF), &p.tmap_q, qx, q_row, fb);
-      tma_load_2d(smem_u32(smem + Q_OFF + BOX_BYTES), &p.tmap_q, qx + 64, q_row, fb);
-      // issue order: K_0, then {K_{j+1}, V_j}: K runs one tile ahead of V
-      int nk = 0, nv = 0;   // tiles issued
-      bool ok = true;
-      auto load_k = [&](int j) -> bool {
+      mbar_expect_tx(fb, 2 * TILE_BYTES);
+      for (int t = 0; t < 2; ++t) {
+        uint8_t* dst = smem + Q_OFF + t * TILE_BYTES;
+        tma_load_2d(smem_u32(dst), &p.tmap_q, qx, q_row + t * BQ, fb);
+        tma_load_2d(smem_u32(dst + BOX_BYTES), &p.tmap_q, qx + 64, q_row + t * BQ, fb);
+      }
+      int nk = 0, nv = 0;
+      auto load = [&](int j, bool is_v) -> bool {
         const int s = j & 1;
-        if (j >= 2 && !mbar_wait(smem_u32(&k_empty[s]), ((j >> 1) - 1) & 1, abort_flag)) return false;
-        const uint32_t b = smem_u32(&k_full[s]);
+        uint64_t* empty = is_v ? v_empty : k_empty;
+        uint64_t* full = is_v ? v_full : k_full;
+        if (j >= 2 && !mbar_wait(smem_u32(&empty[s]), ((j >> 1) - 1) & 1, abort_flag)) return false;
+        const uint32_t b = smem_u32(&full[s]);
         mbar_expect_tx(b, TILE_BYTES);
-        uint8_t* dst = smem + K_OFF + s * TILE_BYTES;
-        tma_load_2d(smem_u32(dst), &p.tmap_kv, kx, row0 + j * BK, b);
-        tma_load_2d(smem_u32(dst + BOX_BYTES), &p.tmap_kv, kx + 64, row0 + j * BK, b);
-        ++nk;
+        uint8_t* dst = smem + (is_v ? V_OFF : K_OFF) + s * TILE_BYTES;
+        const int x = is_v ? vx : kx;
+        tma_load_2d(smem_u32(dst), &p.tmap_kv, x, row0 + j * BK, b);
+        tma_load_2d(smem_u32(dst + BOX_BYTES), &p.tmap_kv, x + 64, row0 + j * BK, b);
+        if (is_v) ++nv; else ++nk;
         return true;
       };
-      auto load_v = [&](int j) -> bool {
-        const int s = j & 1;
-        if (j >= 2 && !mbar_wait(smem_u32(&v_empty[s]), ((j >> 1) - 1) & 1, abort_flag)) return false;
-        const uint32_t b = smem_u32(&v_full[s]);
-        mbar_expect_tx(b, TILE_BYTES);
-        uint8_t* dst = smem + V_OFF + s * TILE_BYTES;
-        tma_load_2d(smem_u32(dst), &p.tmap_kv, vx, row0 + j * BK, b);
-        tma_load_2d(smem_u32(dst + BOX_BYTES), &p.tmap_kv, vx + 64, row0 + j * BK, b);
-        ++nv;
-        return true;
-      };
-      ok = load_k(0);
+      // K runs one tile ahead of V (QK_X(j+1) is issued before PV_X(j+1))
+      bool ok = load(0, false);
       for (int j = 0; j < n_kv && ok; ++j) {
-        if (j + 1 < n_kv) ok = load_k(j + 1);
-        if (ok) ok = load_v(j);
+        if (j + 1 < n_kv) ok = load(j + 1, false);
+        if (ok) ok = load(j, true);
       }
       if (!ok) {
         fail();
-        // let every copy in flight land before the CTA can exit
         mbar_wait(smem_u32(q_full), 0, nullptr);
         for (int j = nk > 2 ? nk - 2 : 0; j < nk; ++j)
           mbar_wait(smem_u32(&k_full[j & 1]), (j >> 1) & 1, nullptr);
@@ -190,59 +288,66 @@ __global__ void __launch_bounds__(THREADS, 1) k_fmha(const __grid_constant__ Arg
           mbar_wait(smem_u32(&v_full[j & 1]), (j >> 1) & 1, nullptr);
       }
     }
-  } else if (warp == 1) {
+  } else if (warp == 9) {
     if (lane == 0) {
-      const uint32_t q_s = smem_u32(smem + Q_OFF);
-      auto issue_qk = [&](int j) {
+      auto issue_qk = [&](int t, int j) {
+        const uint32_t q_s = smem_u32(smem + Q_OFF + t * TILE_BYTES);
         const uint32_t k_s = smem_u32(smem + K_OFF + (j & 1) * TILE_BYTES);
-        const uint32_t d = tmem + (uint32_t)(j % 3) * 128;
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {
           const uint32_t off = (kk >> 2) * BOX_BYTES + (kk & 3) * 32;   // 16 head dims
-          tc_mma_bf16_ss(d, desc_kmajor_sw128(q_s + off), desc_kmajor_sw128(k_s + off), IDESC_QK,
-                         kk != 0);
+          tc_mma_bf16_ss(tmem + s_col(t), desc_kmajor_sw128(q_s + off),
+                         desc_kmajor_sw128(k_s + off), IDESC_QK, kk != 0);
         }
-        tc_commit(smem_u32(&s_full[j % 3]));
-        tc_commit(smem_u32(&k_empty[j & 1]));
+        tc_commit(smem_u32(&s_full[t]));
       };
-      bool ok = mbar_wait(smem_u32(q_full), 0, abort_flag) &&
-                mbar_wait(smem_u32(&k_full[0]), 0, abort_flag);
-      if (ok) {
-        tc_fence_after();
-        issue_qk(0);
-      }
-      for (int j = 0; j < n_kv && ok; ++j) {
-        if (j + 1 < n_kv) {
-          const int jn = j + 1;
-          // S buffer jn % 3 last held P_{jn-3}: its P V must be done
-          if (jn >= 3 && !mbar_wait(smem_u32(&pv_done[jn % 3]), ((jn - 3) / 3) & 1, abort_flag)) {
-            ok = false;
-            break;
-          }
-          if (!mbar_wait(smem_u32(&k_full[jn & 1]), (jn >> 1) & 1, abort_flag)) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          issue_qk(jn);
-        }
-        if (!mbar_wait(smem_u32(&p_full[j % 3]), (j / 3) & 1, abort_flag) ||
-            !mbar_wait(smem_u32(&v_full[j & 1]), (j >> 1) & 1, abort_flag)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-        const uint32_t p_t = tmem + (uint32_t)(j % 3) * 128;
+      auto issue_pv = [&](int t, int j) {
         const uint32_t v_s = smem_u32(smem + V_OFF + (j & 1) * TILE_BYTES);
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {
           // 16 keys: P columns kk*8.. (bf16 pairs), V rows kk*16.. (MN-major:
           // 64-dim chunks LBO = 16 KiB apart, 8-row groups SBO = 1 KiB apart)
-          tc_mma_bf16_ts(tmem + O_COL, p_t + kk * 8, smem_desc(v_s + kk * 2048, BOX_BYTES, 1024, 2),
-                         IDESC_PV, (j | kk) != 0);
+          tc_mma_bf16_ts(tmem + o_col(t), tmem + s_col(t) + kk * 8,
+                         smem_desc(v_s + kk * 2048, BOX_BYTES, 1024, 2), IDESC_PV, (j | kk) != 0);
         }
+        tc_commit(smem_u32(&pv_done[t]));
+      };
+      bool ok = mbar_wait(smem_u32(q_full), 0, abort_flag) &&
+                mbar_wait(smem_u32(&k_full[0]), 0, abort_flag);
+      if (ok) {
+        tc_fence_after();
+        issue_qk(0, 0);
+        issue_qk(1, 0);
+        tc_commit(smem_u32(&k_empty[0]));
+      }
+      for (int j = 0; j < n_kv && ok; ++j) {
+        const bool more = j + 1 < n_kv;
+        if (!mbar_wait(smem_u32(&v_full[j & 1]), (j >> 1) & 1, abort_flag) ||
+            !mbar_wait(smem_u32(&p_full[0]), j & 1, abort_flag)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        issue_pv(0, j);
+        if (more) {
+          if (!mbar_wait(smem_u32(&k_full[(j + 1) & 1]), ((j + 1) >> 1) & 1, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          issue_qk(0, j + 1);
+        }
+        if (!mbar_wait(smem_u32(&p_full[1]), j & 1, abort_flag)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        issue_pv(1, j);
         tc_commit(smem_u32(&v_empty[j & 1]));
-        tc_commit(smem_u32(&pv_done[j % 3]));
+        if (more) {
+          issue_qk(1, j + 1);
+          tc_commit(smem_u32(&k_empty[(j + 1) & 1]));
+        }
       }
       if (!ok) {
         fail();
@@ -250,109 +355,113 @@ __global__ void __launch_bounds__(THREADS, 1) k_fmha(const __grid_constant__ Arg
         mbar_wait(smem_u32(drain), 0, nullptr);
       }
     }
+   }
+    tc_fence_before();
+    named_barrier_sync(1, THREADS);
+    if (warp == 9) {
+      __syncwarp();
+      tc_fence_after();
+      tmem_dealloc(tmem, TMEM_COLS);
+    }
   } else {
-    // softmax: thread = query row (TMEM lane quadrant warp % 4)
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kSoftmaxRegs));
+    // softmax of tile t: thread = query row (TMEM lane quadrant warp % 4)
+    const int t = warp >> 2;
     const int qd = warp & 3;
     const int r = qd * 32 + lane;
     const uint32_t lane_addr = (uint32_t)(qd * 32) << 16;
+    const uint32_t s_t = tmem + lane_addr + s_col(t);
+    const uint32_t o_t = tmem + lane_addr + o_col(t);
     float m_used = -INFINITY, l = 0.f;
     bool ok = true;
     for (int j = 0; j < n_kv; ++j) {
-      ok = __all_sync(0xffffffffu, mbar_wait(smem_u32(&s_full[j % 3]), (j / 3) & 1, abort_flag));
+      ok = __all_sync(0xffffffffu, mbar_wait(smem_u32(&s_full[t]), j & 1, abort_flag));
       if (!ok) break;
       tc_fence_after();
-      const uint32_t s_t = tmem + lane_addr + (uint32_t)(j % 3) * 128;
+      const int valid = min(BK, len - j * BK);   // keys of this tile inside the document
       uint32_t sv[128];
       tmem_ld_32x32b_x64(s_t, sv);
       tmem_ld_32x32b_x64(s_t + 64, sv + 64);
       tmem_ld_wait();
-      const int valid = min(BK, len - j * BK);   // keys of this tile inside the document
-      float mx = -INFINITY;
+      const bool partial = valid < BK;             // warp-uniform
+      if (partial) {
 #pragma unroll
-      for (int c = 0; c < BK; ++c) {
-        const float t = c < valid ? __uint_as_float(sv[c]) * p.scale_log2 : -INFINITY;
-        sv[c] = __float_as_uint(t);
-        mx = fmaxf(mx, t);
+        for (int c = 0; c < 128; ++c)
+          if (c >= valid) sv[c] = 0xff800000u;     // -inf: masked key
       }
+      // row max of the scaled logits (scale > 0 commutes with max)
+      float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+      for (int c = 0; c < 128; c += 8) {
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+          m4[u] = max3(m4[u], __uint_as_float(sv[c + 2 * u]), __uint_as_float(sv[c + 2 * u + 1]));
+      }
+      const float mx = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3])) * p.scale_log2;
       const float m_new = fmaxf(m_used, mx);
-      if (__any_sync(0xffffffffu, m_new > m_used + kRescaleLog2)) {
-        const float alpha = ex2(m_used - m_new);   // 0 on the first tile (m_used = -inf)
-        if (j > 0) {
-          // O must be final for P_{j-1} before it is rescaled
-          ok = __all_sync(0xffffffffu, mbar_wait(smem_u32(&pv_done[(j - 1) % 3]),
-                                                  ((j - 1) / 3) & 1, abort_flag));
-          if (!ok) break;
-          tc_fence_after();
-#pragma unroll
-          for (int h = 0; h < 4; ++h) {
-            uint32_t ov[32];
-            tmem_ld_32x32b_x32(tmem + lane_addr + O_COL + h * 32, ov);
-            tmem_ld_wait();
-#pragma unroll
-            for (int c = 0; c < 32; ++c) ov[c] = __float_as_uint(__uint_as_float(ov[c]) * alpha);
-            tmem_st_32x32b_x32(tmem + lane_addr + O_COL + h * 32, ov);
-          }
-          tmem_st_wait();
-        }
-        l *= alpha;
+      const bool rescale = __any_sync(0xffffffffu, m_new > m_used + kRescaleLog2);
+      float alpha = 1.f;
+      if (rescale) {
+        alpha = ex2(m_used - m_new);               // 0 on the first tile (m_used = -inf)
         m_used = m_new;
       }
-      float sum = 0.f;
+      // P written over the S columns already read
+      const float2 s2 = partial ? softmax_exp_store<false>(sv, p.scale_log2, m_used, s_t)
+                                : softmax_exp_store<true>(sv, p.scale_log2, m_used, s_t);
+      const float sum = s2.x + s2.y;
+      if (rescale && j > 0) {
+        // O must be final for P(j-1) before it is rescaled (PV(j) waits for p_full)
+        ok = __all_sync(0xffffffffu, mbar_wait(smem_u32(&pv_done[t]), (j - 1) & 1, abort_flag));
+        if (!ok) break;
+        tc_fence_after();
 #pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        uint32_t pk[32];
+        for (int h = 0; h < 4; ++h) {
+          uint32_t ov[32];
+          tmem_ld_32x32b_x32(o_t + h * 32, ov);
+          tmem_ld_wait();
 #pragma unroll
-        for (int c = 0; c < 32; ++c) {
-          const float a = ex2(__uint_as_float(sv[h * 64 + 2 * c]) - m_used);
-          const float b = ex2(__uint_as_float(sv[h * 64 + 2 * c + 1]) - m_used);
-          sum += a + b;
-          pk[c] = pack_bf16x2(a, b);
+          for (int c = 0; c < 32; ++c) ov[c] = __float_as_uint(__uint_as_float(ov[c]) * alpha);
+          tmem_st_32x32b_x32(o_t + h * 32, ov);
         }
-        tmem_st_32x32b_x32(s_t + h * 32, pk);   // P_j over the first 64 columns of S_j
       }
+      l *= alpha;
       l += sum;
       tmem_st_wait();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(smem_u32(&p_full[j % 3]));
+      if (lane == 0) mbar_arrive(smem_u32(&p_full[t]));
     }
     if (ok && n_kv > 0) {
-      ok = __all_sync(0xffffffffu, mbar_wait(smem_u32(&pv_done[(n_kv - 1) % 3]),
-                                              ((n_kv - 1) / 3) & 1, abort_flag));
+      ok = __all_sync(0xffffffffu, mbar_wait(smem_u32(&pv_done[t]), (n_kv - 1) & 1, abort_flag));
     }
     if (!ok) {
       fail();
     } else if (n_kv > 0) {
       tc_fence_after();
       const float inv_l = 1.0f / l;
-      const bool row_ok = qt * BQ + r < q_len;
-      __nv_bfloat16* op = p.out + (size_t)(q_row + r) * p.ldo + (size_t)head * D;
+      const int lr = qp * 2 * BQ + t * BQ + r;      // row within the document's local queries
+      const bool row_ok = lr < q_len;
+      __nv_bfloat16* op = p.out + (size_t)(q_row + t * BQ + r) * p.ldo + (size_t)head * D;
 #pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        uint32_t ov[64];
-        tmem_ld_32x32b_x64(tmem + lane_addr + O_COL + h * 64, ov);
+      for (int h = 0; h < 4; ++h) {
+        uint32_t ov[32];
+        tmem_ld_32x32b_x32(o_t + h * 32, ov);
         tmem_ld_wait();
         if (row_ok) {
 #pragma unroll
-          for (int c = 0; c < 8; ++c) {
+          for (int c = 0; c < 4; ++c) {
             uint4 w;
             w.x = pack_bf16x2(__uint_as_float(ov[8 * c + 0]) * inv_l, __uint_as_float(ov[8 * c + 1]) * inv_l);
             w.y = pack_bf16x2(__uint_as_float(ov[8 * c + 2]) * inv_l, __uint_as_float(ov[8 * c + 3]) * inv_l);
             w.z = pack_bf16x2(__uint_as_float(ov[8 * c + 4]) * inv_l, __uint_as_float(ov[8 * c + 5]) * inv_l);
             w.w = pack_bf16x2(__uint_as_float(ov[8 * c + 6]) * inv_l, __uint_as_float(ov[8 * c + 7]) * inv_l);
-            *reinterpret_cast<uint4*>(op + h * 64 + c * 8) = w;
+            *reinterpret_cast<uint4*>(op + h * 32 + c * 8) = w;
           }
         }
       }
     }
-  }
-
-  tc_fence_before();
-  __syncthreads();
-  if (warp == 1) {
-    __syncwarp();
-    tc_fence_after();
-    tmem_dealloc(tmem, TMEM_COLS);
+    tc_fence_before();
+    named_barrier_sync(1, THREADS);
   }
 }
 

@@ -43,6 +43,12 @@ __device__ __forceinline__ float bf16_bits_to_f32(uint32_t b16) {
 }
 
 // Two fp32 -> packed bf16x2 (round-to-nearest-even), lo in the low half.
+// bar.sync on a named barrier: the threads of several branches meet without a
+// __syncthreads() in code they share.
+__device__ __forceinline__ void named_barrier_sync(int id, int threads) {
+  asm volatile("barrier.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
+
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
   return *reinterpret_cast<uint32_t*>(&v);

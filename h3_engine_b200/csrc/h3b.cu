@@ -425,11 +425,17 @@ int h3b_attention_varlen(const void* q_buf, int64_t q_rows, int64_t q_stride, in
 
   static std::once_flag attr_once;
   static cudaError_t attr_err = cudaSuccess;
+  static int attr_regs = 0;
   std::call_once(attr_once, [] {
     attr_err = cudaFuncSetAttribute(attn::k_fmha, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                     attn::SMEM_BYTES);
+    cudaFuncAttributes fa;
+    if (attr_err == cudaSuccess) attr_err = cudaFuncGetAttributes(&fa, attn::k_fmha);
+    if (attr_err == cudaSuccess) attr_regs = fa.numRegs;
   });
   if (attr_err != cudaSuccess) return H3B_ERR_CUDA;
+  // the kernel's setmaxnreg split assumes this launch register count
+  if (attr_regs != attn::kLaunchRegs) return H3B_ERR_UNSUPPORTED;
 
   attn::Args args;
   memset(&args, 0, sizeof(args));
@@ -464,7 +470,7 @@ int h3b_attention_varlen(const void* q_buf, int64_t q_rows, int64_t q_stride, in
     args.doc_len[i] = cu_seqlens_host[d + 1] - cu_seqlens_host[d];
     args.q_start[i] = (int)(qa - q_row0);
     args.q_len[i] = (int)(qb - qa);
-    items += (int64_t)((args.q_len[i] + attn::BQ - 1) / attn::BQ) * H;
+    items += (int64_t)((args.q_len[i] + 2 * attn::BQ - 1) / (2 * attn::BQ)) * H;
     if (items > INT32_MAX) return H3B_ERR_INVALID_ARG;
     args.item_end[i] = (int)items;
   }
