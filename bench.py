@@ -1,7 +1,7 @@
 """Benchmark of the NVFP4 DiT hot path on B200.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl h3b|reference]
-                    [--workload dit|ffn]
+                    [--workload dit|ffn|attention] [--attn-docs 32760,1024]
 
 Default workload ("dit"): one denoising step of the full multimodal DiT --
 48 blocks (hidden 3072, 24 heads x 128, FFN 12288 GELU/bias, adaLN-zero),
@@ -22,6 +22,11 @@ e2e         = the same metric through Sampler.step with the step's latent rows
 
 "ffn": the DiT FFN sub-block on 32768 tokens x 3072 (FFN 12288), one
 independent shard per GPU (weak scaling, no collective).
+
+"attention": the packed varlen attention kernel alone (24 heads x 128, bf16,
+documents of --attn-docs tokens, default the DiT packing 32760 + 1024) on a
+seeded synthetic q|k|v activation, one replica per GPU; the kernel-level view
+of the attention share of the DiT step and the small case profiled with ncu.
 
 --impl reference: the reference's NVFP4 path cannot run on a CPU (its
 quantizer is in the absent maiku package), so the timed CPU implementation is
@@ -218,6 +223,60 @@ class FFNWorkload:
         self.y_h.copy_(self.y, non_blocking=True)
 
 
+class AttentionWorkload:
+    name = "attention"
+    HEADS, HEAD_DIM = 24, 128
+
+    def __init__(self, dev, world: int, rank: int, docs: list[int]):
+        H, D = self.HEADS, self.HEAD_DIM
+        T = sum(docs)
+        self.cu = [0]
+        for n in docs:
+            self.cu.append(self.cu[-1] + n)
+        g = torch.Generator(device=dev).manual_seed(3000 + rank)
+        self.qkv = torch.randn(T, 3 * H * D, generator=g, device=dev).to(torch.bfloat16)
+        self.out = torch.empty(T, H * D, device=dev, dtype=torch.bfloat16)
+        fl = sum(4 * H * D * n * n for n in docs)
+        self.step_flops = world * fl
+        self.rank_gemm_flops = 0
+        self.rank_attn_flops = fl
+        self.events = None
+        self.config = {"workload": "packed varlen attention (bf16 q|k|v activation, 24 heads x 128, "
+                                   "one softmax(QK^T / sqrt(d)) V per document)",
+                       "documents": self.cu, "heads": H, "head_dim": D,
+                       "parallelism": f"replicas x{world}",
+                       "l2": f"q|k|v {self.qkv.numel() * 2 / 1e6:.0f} MB per launch"}
+
+    def set_timers(self, gemm, attn):
+        self.events = attn
+
+    def _run(self, qkv):
+        from h3_engine_b200 import ops
+        H, D = self.HEADS, self.HEAD_DIM
+        if self.events is not None:
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+        ops.attention_varlen(qkv, H, D, self.cu, q_off=0, k_off=H * D, v_off=2 * H * D,
+                             out=self.out)
+        if self.events is not None:
+            b.record()
+            self.events.append((a, b))
+
+    def step(self):
+        self._run(self.qkv)
+
+    def e2e_setup(self):
+        self.x_h = self.qkv.cpu().pin_memory()
+        self.y_h = torch.empty_like(self.out, device="cpu").pin_memory()
+        self.x_d = torch.empty_like(self.qkv)
+        return self.x_h.numel() * 2, self.y_h.numel() * 2
+
+    def e2e_step(self):
+        self.x_d.copy_(self.x_h, non_blocking=True)
+        self._run(self.x_d)
+        self.y_h.copy_(self.out, non_blocking=True)
+
+
 # ----------------------------------------------------------------------------- CPU
 def cpu_dit_estimate(sample_rows: int) -> dict:
     """Extrapolated CPU time of the DiT step from a sample of query rows: the
@@ -276,6 +335,10 @@ def run_reference(args) -> None:
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
+    if args.workload == "attention":
+        print(json.dumps({"impl": "reference", "unavailable": "the attention-only profiling "
+                          "workload has no CPU arm; the dit and ffn workloads have one"}), flush=True)
+        return
     vals = []
     for _ in range(max(args.steps, 1)):
         r = cpu_dit_estimate(args.cpu_rows) if args.workload == "dit" else cpu_ffn_run(args.cpu_rows)
@@ -311,7 +374,12 @@ def run_ours(args) -> None:
         if world > 1:
             dist.barrier()
 
-    wl = DiTWorkload(dev, world, rank) if args.workload == "dit" else FFNWorkload(dev, world, rank)
+    if args.workload == "dit":
+        wl = DiTWorkload(dev, world, rank)
+    elif args.workload == "ffn":
+        wl = FFNWorkload(dev, world, rank)
+    else:
+        wl = AttentionWorkload(dev, world, rank, [int(n) for n in args.attn_docs.split(",")])
     for _ in range(args.warmup):
         wl.step()
     torch.cuda.synchronize()
@@ -363,7 +431,7 @@ def run_ours(args) -> None:
     extras = {}
     if rank == 0 and not args.no_extras:
         extras["library_gemm_torch_scaled_mm"] = library_gemm_reference(dev)
-        if world == 1:
+        if world == 1 and args.workload != "attention":
             cpu = (cpu_dit_estimate(args.cpu_rows) if args.workload == "dit"
                    else cpu_ffn_run(args.cpu_rows))
             extras["cpu_baseline"] = {k: cpu[k] for k in ("value", "unit", "cores", "kind", "sample")}
@@ -458,7 +526,9 @@ def main() -> None:
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["h3b", "reference"], default="h3b")
-    ap.add_argument("--workload", choices=["dit", "ffn"], default="dit")
+    ap.add_argument("--workload", choices=["dit", "ffn", "attention"], default="dit")
+    ap.add_argument("--attn-docs", default="32760,1024",
+                    help="document lengths of the attention workload (comma-separated)")
     ap.add_argument("--cpu-rows", type=int, default=64,
                     help="query rows (dit) / tokens (ffn) of the CPU sample")
     ap.add_argument("--no-extras", action="store_true",

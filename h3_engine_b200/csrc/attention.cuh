@@ -9,10 +9,11 @@
 //
 // One CTA = two 128-row query tiles (A, B) of one head of one document; K/V
 // tiles are loaded once for both:
-//   warp 8      TMA producer: Q_A, Q_B once, then K and V tiles (128 rows x 128)
-//               into two separate 2-stage rings, read straight from the q / kv
-//               activations.
-//   warp 9      TMEM allocator + single-thread MMA issuer.  One in-order MMA
+//   warp 8      TMA producer: Q_A, Q_B and K(0) once, then V(j) with K(j+1)
+//               into 2-stage rings, read straight from the q / kv activations,
+//               with L2 prefetches a few tiles ahead.
+//   warp 9      TMEM allocator + MMA issuer (the whole warp runs the issue
+//               loop, one elected lane issues each op).  One in-order MMA
 //               stream, staggered so the tensor core works on one tile while
 //               the other tile's softmax runs:
 //                 QK_A(0) QK_B(0) | PV_A(j) QK_A(j+1) PV_B(j) QK_B(j+1) | ...
@@ -53,8 +54,8 @@ constexpr int THREADS = 384;       // three warpgroups: softmax A, softmax B, pr
 // down to kCtrlRegs so the two softmax warpgroups can hold a whole 128-key row
 // of S: 128 * kCtrlRegs + 256 * kSoftmaxRegs == THREADS * kLaunchRegs.
 constexpr int kLaunchRegs = 168;
-constexpr int kCtrlRegs = 56;
-constexpr int kSoftmaxRegs = 224;
+constexpr int kCtrlRegs = 72;
+constexpr int kSoftmaxRegs = 216;
 static_assert(128 * kCtrlRegs + 256 * kSoftmaxRegs <= THREADS * kLaunchRegs, "register split");
 constexpr uint32_t TMEM_COLS = 512;
 __host__ __device__ constexpr uint32_t s_col(int t) { return (uint32_t)t * 128u; }
@@ -66,6 +67,7 @@ constexpr uint32_t IDESC_QK = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(B
 // P V: B = V is MN-major (head dim contiguous): bit 16
 constexpr uint32_t IDESC_PV = IDESC_QK | (1u << 16);
 constexpr float kRescaleLog2 = 8.0f;
+constexpr int kPrefetchTiles = 4;     // K / V tiles warmed in L2 ahead of the loads
 
 static_assert(SMEM_BYTES <= 232448, "shared memory budget");
 
@@ -144,19 +146,19 @@ __device__ __forceinline__ float2 ex2_poly2(float2 x) {
 // use the MUFU ex2 unit (16 results per clock per SM).
 constexpr uint32_t kPolyPairs = 0x52u;   // pairs 1, 4, 6
 
-// P = 2^(S * scale_log2 - m) for one 128-key row held in registers, packed to
-// bf16 pairs and stored over the first 64 columns of the row's S in tensor
-// memory; returns the row sum (two lanes).  MIXED splits the exponentials
-// between MUFU and the polynomial; the partial last tile of a document uses
-// MUFU only, where a masked key (S = -inf) gives exactly 0.
-template <bool MIXED>
-__device__ __forceinline__ float2 softmax_exp_store(uint32_t (&sv)[128], float scale_log2,
-                                                    float m, uint32_t s_addr) {
+// P = 2^(S * scale_log2 - m) for NC keys of one row held in registers, packed
+// to bf16 pairs and stored over NC / 2 columns of the row's S in tensor
+// memory from s_addr; returns the sum (two lanes).  MIXED splits the
+// exponentials between MUFU and the polynomial; a partial last tile of a
+// document uses MUFU only, where a masked key (S = -inf) gives exactly 0.
+template <int NC, bool MIXED>
+__device__ __forceinline__ float2 softmax_exp_store(uint32_t (&sv)[NC], float scale_log2, float m,
+                                                    uint32_t s_addr) {
   const float2 sc = make_float2(scale_log2, scale_log2);
   const float2 nm = make_float2(-m, -m);
   float2 acc0 = make_float2(0.f, 0.f), acc1 = make_float2(0.f, 0.f);
 #pragma unroll
-  for (int h = 0; h < 2; ++h) {
+  for (int h = 0; h < NC / 64; ++h) {
     uint32_t pk[32];
 #pragma unroll
     for (int c = 0; c < 32; ++c) {
@@ -182,15 +184,19 @@ __global__ void __launch_bounds__(THREADS, 1) k_fmha(const __grid_constant__ Arg
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + BAR_OFF);
+  // q_full: Q_A, Q_B and K(0).  kv_full[j % 2]: V(j) and K(j + 1), loaded
+  // together.  kv_empty[j % 2]: released by the commit after QK_B(j + 1),
+  // which follows PV_B(j) (frees V stage j % 2 and K stage (j + 1) % 2; the
+  // prologue's release of K(0) counts as j = -1).  pv_done: the last PV of a
+  // tile (the next QK commit already implies every earlier PV, tcgen05 ops of
+  // one thread completing in issue order).
   uint64_t* q_full = bars;           // 1
-  uint64_t* k_full = bars + 1;       // 2
-  uint64_t* k_empty = bars + 3;      // 2
-  uint64_t* v_full = bars + 5;       // 2
-  uint64_t* v_empty = bars + 7;      // 2
-  uint64_t* s_full = bars + 9;       // 2 (tile A, B)
-  uint64_t* p_full = bars + 11;      // 2
-  uint64_t* pv_done = bars + 13;     // 2
-  uint64_t* drain = bars + 15;       // 1
+  uint64_t* kv_full = bars + 1;      // 2
+  uint64_t* kv_empty = bars + 3;     // 2
+  uint64_t* s_full = bars + 5;       // 2 (tile A, B)
+  uint64_t* p_full = bars + 7;       // 2
+  uint64_t* pv_done = bars + 9;      // 2
+  uint64_t* drain = bars + 11;       // 1
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
@@ -213,10 +219,8 @@ __global__ void __launch_bounds__(THREADS, 1) k_fmha(const __grid_constant__ Arg
   if (threadIdx.x == 0) {
     mbar_init(smem_u32(q_full), 1);
     for (int i = 0; i < 2; ++i) {
-      mbar_init(smem_u32(&k_full[i]), 1);
-      mbar_init(smem_u32(&k_empty[i]), 1);
-      mbar_init(smem_u32(&v_full[i]), 1);
-      mbar_init(smem_u32(&v_empty[i]), 1);
+      mbar_init(smem_u32(&kv_full[i]), 1);
+      mbar_init(smem_u32(&kv_empty[i]), 1);
       mbar_init(smem_u32(&s_full[i]), 1);
       mbar_init(smem_u32(&p_full[i]), 4);
       mbar_init(smem_u32(&pv_done[i]), 1);
@@ -252,109 +256,119 @@ __global__ void __launch_bounds__(THREADS, 1) k_fmha(const __grid_constant__ Arg
       prefetch_tmap(&p.tmap_kv);
       const int qx = p.q_off + head * D, kx = p.k_off + head * D, vx = p.v_off + head * D;
       uint32_t fb = smem_u32(q_full);
-      mbar_expect_tx(fb, 2 * TILE_BYTES);
+      mbar_expect_tx(fb, 3 * TILE_BYTES);
       for (int t = 0; t < 2; ++t) {
         uint8_t* dst = smem + Q_OFF + t * TILE_BYTES;
         tma_load_2d(smem_u32(dst), &p.tmap_q, qx, q_row + t * BQ, fb);
         tma_load_2d(smem_u32(dst + BOX_BYTES), &p.tmap_q, qx + 64, q_row + t * BQ, fb);
       }
-      int nk = 0, nv = 0;
-      auto load = [&](int j, bool is_v) -> bool {
-        const int s = j & 1;
-        uint64_t* empty = is_v ? v_empty : k_empty;
-        uint64_t* full = is_v ? v_full : k_full;
-        if (j >= 2 && !mbar_wait(smem_u32(&empty[s]), ((j >> 1) - 1) & 1, abort_flag)) return false;
-        const uint32_t b = smem_u32(&full[s]);
-        mbar_expect_tx(b, TILE_BYTES);
-        uint8_t* dst = smem + (is_v ? V_OFF : K_OFF) + s * TILE_BYTES;
-        const int x = is_v ? vx : kx;
-        tma_load_2d(smem_u32(dst), &p.tmap_kv, x, row0 + j * BK, b);
-        tma_load_2d(smem_u32(dst + BOX_BYTES), &p.tmap_kv, x + 64, row0 + j * BK, b);
-        if (is_v) ++nv; else ++nk;
-        return true;
+      tma_load_2d(smem_u32(smem + K_OFF), &p.tmap_kv, kx, row0, fb);
+      tma_load_2d(smem_u32(smem + K_OFF + BOX_BYTES), &p.tmap_kv, kx + 64, row0, fb);
+      // K / V tiles are first touched by all CTAs of a head at about the same
+      // time; L2 prefetches kPrefetchTiles ahead hide the DRAM latency that
+      // the two-stage shared-memory ring cannot.
+      auto prefetch = [&](int j) {
+        if (j < n_kv) {
+          tma_prefetch_2d(&p.tmap_kv, kx, row0 + j * BK);
+          tma_prefetch_2d(&p.tmap_kv, kx + 64, row0 + j * BK);
+          tma_prefetch_2d(&p.tmap_kv, vx, row0 + j * BK);
+          tma_prefetch_2d(&p.tmap_kv, vx + 64, row0 + j * BK);
+        }
       };
-      // K runs one tile ahead of V (QK_X(j+1) is issued before PV_X(j+1))
-      bool ok = load(0, false);
-      for (int j = 0; j < n_kv && ok; ++j) {
-        if (j + 1 < n_kv) ok = load(j + 1, false);
-        if (ok) ok = load(j, true);
+      for (int j = 1; j < kPrefetchTiles; ++j) prefetch(j);
+      int issued = 0;
+      bool ok = true;
+      for (int j = 0; j < n_kv; ++j) {
+        prefetch(j + kPrefetchTiles);
+        if (j >= 1) {
+          // release r = j - 2 frees K stage (j + 1) % 2 and V stage j % 2
+          const int r = j - 2;
+          const int st = r & 1;
+          const int completion = st ? (r + 1) >> 1 : r >> 1;
+          if (!mbar_wait(smem_u32(&kv_empty[st]), completion & 1, abort_flag)) {
+            ok = false;
+            break;
+          }
+        }
+        const bool more = j + 1 < n_kv;
+        const uint32_t b = smem_u32(&kv_full[j & 1]);
+        mbar_expect_tx(b, more ? 2 * TILE_BYTES : TILE_BYTES);
+        uint8_t* vdst = smem + V_OFF + (j & 1) * TILE_BYTES;
+        tma_load_2d(smem_u32(vdst), &p.tmap_kv, vx, row0 + j * BK, b);
+        tma_load_2d(smem_u32(vdst + BOX_BYTES), &p.tmap_kv, vx + 64, row0 + j * BK, b);
+        if (more) {
+          uint8_t* kdst = smem + K_OFF + ((j + 1) & 1) * TILE_BYTES;
+          tma_load_2d(smem_u32(kdst), &p.tmap_kv, kx, row0 + (j + 1) * BK, b);
+          tma_load_2d(smem_u32(kdst + BOX_BYTES), &p.tmap_kv, kx + 64, row0 + (j + 1) * BK, b);
+        }
+        ++issued;
       }
       if (!ok) {
+        // no copy may still be landing when the CTA exits
         fail();
         mbar_wait(smem_u32(q_full), 0, nullptr);
-        for (int j = nk > 2 ? nk - 2 : 0; j < nk; ++j)
-          mbar_wait(smem_u32(&k_full[j & 1]), (j >> 1) & 1, nullptr);
-        for (int j = nv > 2 ? nv - 2 : 0; j < nv; ++j)
-          mbar_wait(smem_u32(&v_full[j & 1]), (j >> 1) & 1, nullptr);
+        for (int j = issued > 2 ? issued - 2 : 0; j < issued; ++j)
+          mbar_wait(smem_u32(&kv_full[j & 1]), (j >> 1) & 1, nullptr);
       }
     }
   } else if (warp == 9) {
-    if (lane == 0) {
+      // The whole warp runs the issue loop on warp-uniform values; each
+      // tcgen05 op is issued by one elected lane.
+      auto wait = [&](uint64_t* bar, uint32_t parity) -> bool {
+        return __all_sync(0xffffffffu, mbar_wait(smem_u32(bar), parity, abort_flag));
+      };
+      // descriptors advance by adding (byte offset >> 4) to the start-address
+      // field (shared-memory addresses stay below 256 KiB: no carry out)
       auto issue_qk = [&](int t, int j) {
-        const uint32_t q_s = smem_u32(smem + Q_OFF + t * TILE_BYTES);
-        const uint32_t k_s = smem_u32(smem + K_OFF + (j & 1) * TILE_BYTES);
+        const uint64_t qd = desc_kmajor_sw128(smem_u32(smem + Q_OFF + t * TILE_BYTES));
+        const uint64_t kd = desc_kmajor_sw128(smem_u32(smem + K_OFF + (j & 1) * TILE_BYTES));
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {
-          const uint32_t off = (kk >> 2) * BOX_BYTES + (kk & 3) * 32;   // 16 head dims
-          tc_mma_bf16_ss(tmem + s_col(t), desc_kmajor_sw128(q_s + off),
-                         desc_kmajor_sw128(k_s + off), IDESC_QK, kk != 0);
+          const uint32_t off = ((kk >> 2) * BOX_BYTES + (kk & 3) * 32) >> 4;   // 16 head dims
+          tc_mma_bf16_ss_elect(tmem + s_col(t), qd + off, kd + off, IDESC_QK, kk != 0);
         }
-        tc_commit(smem_u32(&s_full[t]));
+        tc_commit_elect(smem_u32(&s_full[t]));
       };
       auto issue_pv = [&](int t, int j) {
-        const uint32_t v_s = smem_u32(smem + V_OFF + (j & 1) * TILE_BYTES);
+        // 16 keys per MMA: P columns kk*8.. (bf16 pairs), V rows kk*16..
+        // (MN-major: 64-dim chunks LBO = 16 KiB apart, 8-row groups SBO = 1 KiB)
+        const uint64_t vd = smem_desc(smem_u32(smem + V_OFF + (j & 1) * TILE_BYTES), BOX_BYTES, 1024, 2);
 #pragma unroll
-        for (int kk = 0; kk < 8; ++kk) {
-          // 16 keys: P columns kk*8.. (bf16 pairs), V rows kk*16.. (MN-major:
-          // 64-dim chunks LBO = 16 KiB apart, 8-row groups SBO = 1 KiB apart)
-          tc_mma_bf16_ts(tmem + o_col(t), tmem + s_col(t) + kk * 8,
-                         smem_desc(v_s + kk * 2048, BOX_BYTES, 1024, 2), IDESC_PV, (j | kk) != 0);
-        }
-        tc_commit(smem_u32(&pv_done[t]));
+        for (int kk = 0; kk < 8; ++kk)
+          tc_mma_bf16_ts_elect(tmem + o_col(t), tmem + s_col(t) + kk * 8, vd + kk * (2048 >> 4),
+                               IDESC_PV, (j | kk) != 0);
+        if (j + 1 == n_kv) tc_commit_elect(smem_u32(&pv_done[t]));
       };
-      bool ok = mbar_wait(smem_u32(q_full), 0, abort_flag) &&
-                mbar_wait(smem_u32(&k_full[0]), 0, abort_flag);
+      bool ok = wait(q_full, 0);
       if (ok) {
         tc_fence_after();
         issue_qk(0, 0);
         issue_qk(1, 0);
-        tc_commit(smem_u32(&k_empty[0]));
+        tc_commit_elect(smem_u32(&kv_empty[1]));        // release of K(0)
       }
       for (int j = 0; j < n_kv && ok; ++j) {
         const bool more = j + 1 < n_kv;
-        if (!mbar_wait(smem_u32(&v_full[j & 1]), (j >> 1) & 1, abort_flag) ||
-            !mbar_wait(smem_u32(&p_full[0]), j & 1, abort_flag)) {
+        if (!wait(&kv_full[j & 1], (j >> 1) & 1) || !wait(&p_full[0], j & 1)) {
           ok = false;
           break;
         }
         tc_fence_after();
         issue_pv(0, j);
-        if (more) {
-          if (!mbar_wait(smem_u32(&k_full[(j + 1) & 1]), ((j + 1) >> 1) & 1, abort_flag)) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          issue_qk(0, j + 1);
-        }
-        if (!mbar_wait(smem_u32(&p_full[1]), j & 1, abort_flag)) {
+        if (more) issue_qk(0, j + 1);
+        if (!wait(&p_full[1], j & 1)) {
           ok = false;
           break;
         }
         tc_fence_after();
         issue_pv(1, j);
-        tc_commit(smem_u32(&v_empty[j & 1]));
-        if (more) {
-          issue_qk(1, j + 1);
-          tc_commit(smem_u32(&k_empty[(j + 1) & 1]));
-        }
+        if (more) issue_qk(1, j + 1);
+        tc_commit_elect(smem_u32(&kv_empty[j & 1]));
       }
       if (!ok) {
-        fail();
-        tc_commit(smem_u32(drain));
+        if (lane == 0) fail();
+        tc_commit_elect(smem_u32(drain));
         mbar_wait(smem_u32(drain), 0, nullptr);
       }
-    }
    }
     tc_fence_before();
     named_barrier_sync(1, THREADS);
@@ -406,14 +420,11 @@ __global__ void __launch_bounds__(THREADS, 1) k_fmha(const __grid_constant__ Arg
         m_used = m_new;
       }
       // P written over the S columns already read
-      const float2 s2 = partial ? softmax_exp_store<false>(sv, p.scale_log2, m_used, s_t)
-                                : softmax_exp_store<true>(sv, p.scale_log2, m_used, s_t);
-      const float sum = s2.x + s2.y;
+      const float2 s2 = partial ? softmax_exp_store<128, false>(sv, p.scale_log2, m_used, s_t)
+                                : softmax_exp_store<128, true>(sv, p.scale_log2, m_used, s_t);
       if (rescale && j > 0) {
-        // O must be final for P(j-1) before it is rescaled (PV(j) waits for p_full)
-        ok = __all_sync(0xffffffffu, mbar_wait(smem_u32(&pv_done[t]), (j - 1) & 1, abort_flag));
-        if (!ok) break;
-        tc_fence_after();
+        // O is final for P(j-1): QK(j), whose completion s_full signalled, was
+        // issued after PV(j-1); PV(j) waits for p_full
 #pragma unroll
         for (int h = 0; h < 4; ++h) {
           uint32_t ov[32];
@@ -424,15 +435,14 @@ __global__ void __launch_bounds__(THREADS, 1) k_fmha(const __grid_constant__ Arg
           tmem_st_32x32b_x32(o_t + h * 32, ov);
         }
       }
-      l *= alpha;
-      l += sum;
+      l = l * alpha + (s2.x + s2.y);
       tmem_st_wait();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(smem_u32(&p_full[t]));
     }
     if (ok && n_kv > 0) {
-      ok = __all_sync(0xffffffffu, mbar_wait(smem_u32(&pv_done[t]), (n_kv - 1) & 1, abort_flag));
+      ok = __all_sync(0xffffffffu, mbar_wait(smem_u32(&pv_done[t]), 0, abort_flag));
     }
     if (!ok) {
       fail();

@@ -172,55 +172,59 @@ __global__ void __launch_bounds__(THREADS, 1) k_gemm_nvfp4(const __grid_constant
       }
     }
   } else if (warp == 1) {
-    if (lane == 0) {
-      uint32_t g = 0, i = 0;
-      bool ok = true;
-      for (int t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x, ++i) {
-        if (i > 0 && !mbar_wait(smem_u32(acc_empty), (i - 1) & 1, abort_flag)) {
+    // The whole warp runs the issue loop on warp-uniform values; one elected
+    // lane issues each tcgen05 op (a converged issuer keeps pace beside the
+    // busy epilogue warps).  Descriptors advance by adding (offset >> 4) to
+    // the start-address field.
+    auto wait = [&](uint64_t* bar, uint32_t parity) -> bool {
+      return __all_sync(0xffffffffu, mbar_wait(smem_u32(bar), parity, abort_flag));
+    };
+    uint32_t g = 0, i = 0;
+    bool ok = true;
+    for (int t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x, ++i) {
+      if (i > 0 && !wait(acc_empty, (i - 1) & 1)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      for (int kb = 0; kb < num_kb; ++kb, ++g) {
+        const int s = g % STAGES;
+        const uint32_t ph = (g / STAGES) & 1;
+        if (!wait(&full[s], ph)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        for (int kb = 0; kb < num_kb; ++kb, ++g) {
-          const int s = g % STAGES;
-          const uint32_t ph = (g / STAGES) & 1;
-          if (!mbar_wait(smem_u32(&full[s]), ph, abort_flag)) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          // Scale atoms of this k-block -> tensor memory (one 32x128b.warpx4
-          // copy per 128 rows per MMA k-step), then the four MMAs that read them.
-          const uint32_t sf_t = tmem + SF_COL + s * SF_STAGE_COLS;
-          const uint32_t sfa_s = smem_u32(sSFA(s));
-          const uint32_t sfb_s = smem_u32(sSFB(s));
+        // Scale atoms of this k-block -> tensor memory (one 32x128b.warpx4
+        // copy per 128 rows per MMA k-step), then the four MMAs that read them.
+        const uint32_t sf_t = tmem + SF_COL + s * SF_STAGE_COLS;
+        const uint64_t sfa_d = desc_sf_atom(smem_u32(sSFA(s)));
+        const uint64_t sfb_d = desc_sf_atom(smem_u32(sSFB(s)));
 #pragma unroll
-          for (int kk = 0; kk < 4; ++kk) {
-            tc_cp_32x128b_warpx4(sf_t + kk * 4, desc_sf_atom(sfa_s + kk * SF_ATOM));
-            tc_cp_32x128b_warpx4(sf_t + 16 + kk * 8, desc_sf_atom(sfb_s + kk * SF_ATOM));
-            tc_cp_32x128b_warpx4(sf_t + 16 + kk * 8 + 4,
-                                 desc_sf_atom(sfb_s + 4 * SF_ATOM + kk * SF_ATOM));
-          }
-          const uint32_t a_s = smem_u32(sA(s)), b_s = smem_u32(sB(s));
+        for (int kk = 0; kk < 4; ++kk) {
+          tc_cp_32x128b_warpx4_elect(sf_t + kk * 4, sfa_d + ((kk * SF_ATOM) >> 4));
+          tc_cp_32x128b_warpx4_elect(sf_t + 16 + kk * 8, sfb_d + ((kk * SF_ATOM) >> 4));
+          tc_cp_32x128b_warpx4_elect(sf_t + 16 + kk * 8 + 4, sfb_d + (((4 + kk) * SF_ATOM) >> 4));
+        }
+        const uint64_t a_d = desc_kmajor_sw128(smem_u32(sA(s)));
+        const uint64_t b_d = desc_kmajor_sw128(smem_u32(sB(s)));
 #pragma unroll
-          for (int kk = 0; kk < 4; ++kk) {
-            tc_mma_nvf4(tmem + ACC_COL, desc_kmajor_sw128(a_s + kk * 32),
-                        desc_kmajor_sw128(b_s + kk * 32), IDESC, sf_t + kk * 4,
-                        sf_t + 16 + kk * 8, (kb | kk) != 0);
-          }
-          tc_commit(smem_u32(&empty[s]));
+        for (int kk = 0; kk < 4; ++kk) {
+          tc_mma_nvf4_elect(tmem + ACC_COL, a_d + ((kk * 32) >> 4), b_d + ((kk * 32) >> 4), IDESC,
+                            sf_t + kk * 4, sf_t + 16 + kk * 8, (kb | kk) != 0);
         }
-        if (!ok) break;
-        tc_commit(smem_u32(acc_full));
+        tc_commit_elect(smem_u32(&empty[s]));
       }
-      if (!ok) {
-        if (!*abort_flag) {
-          record_error(H3B_ERR_TIMEOUT);
-          *abort_flag = 1;
-        }
-        tc_commit(smem_u32(drain));
-        mbar_wait(smem_u32(drain), 0, nullptr);
+      if (!ok) break;
+      tc_commit_elect(smem_u32(acc_full));
+    }
+    if (!ok) {
+      if (lane == 0 && !*abort_flag) {
+        record_error(H3B_ERR_TIMEOUT);
+        *abort_flag = 1;
       }
+      tc_commit_elect(smem_u32(drain));
+      mbar_wait(smem_u32(drain), 0, nullptr);
     }
   } else {
     const int ew = warp - 2;
