@@ -394,7 +394,9 @@ def run_ours(args) -> None:
         e1 = torch.cuda.Event(enable_timing=True)
         e0.record()
         for _ in range(args.steps):
+            torch.cuda.nvtx.range_push("timed_step")     # ncu --nvtx-include "timed_step/"
             wl.step()
+            torch.cuda.nvtx.range_pop()
         e1.record()
         torch.cuda.synchronize()
     barrier()
