@@ -52,10 +52,15 @@ import torch  # noqa: E402
 
 METRIC = "NVFP4 GEMM TFLOP/s/GPU & % FP4 peak; DiT block latency at 1/2/4/8 B200"
 FFN_TOKENS, HIDDEN, FFN = 32768, 3072, 12288
-# Per-launch DRAM traffic of the dominant kernel from the committed ncu
-# summaries (dram__bytes_read.sum + dram__bytes_write.sum); None until captured
-# for the kernel and workload named in the roofline object.
-TRAFFIC_BYTES: dict[str, float | None] = {"k_fmha": None, "k_gemm_nvfp4": None}
+# Per-launch DRAM traffic (dram__bytes_read.sum + dram__bytes_write.sum) of
+# the kernel named in the roofline object, from one ncu capture each:
+#   k_fmha: 183.2 MB at 8192 tokens (q|k|v read once, O written), linear in
+#     tokens -> 2 x 33784 tokens of the DiT attention launch = 1.511 GB; for
+#     the attention workload the same per-token figure times its tokens.
+#   k_gemm_nvfp4: FFN up 835.5 MB, down 639.4 MB at 32768 tokens (mean).
+ATTN_TRAFFIC_PER_TOKEN = (151.128064e6 + 32.116736e6) / 8192
+TRAFFIC_BYTES: dict[str, float | None] = {"k_fmha": ATTN_TRAFFIC_PER_TOKEN * 2 * 33784,
+                                          "k_gemm_nvfp4": (835.5e6 + 639.4e6) / 2}
 
 
 def peaks() -> dict:
@@ -151,6 +156,11 @@ class DiTWorkload:
         self.rank_attn_flops = self.cfg.blocks * branches * sum(
             4 * hd * max(0, min(b, r1) - max(a, r0)) * (b - a) for a, b in doc_of)
         self.attn_launches_per_step = self.cfg.blocks
+        # DRAM bytes of one attention launch on this rank: q rows read once
+        # (6144 B) and their output written (3920 B measured of 6144), every
+        # K|V row of the local branches read once (12288 B)
+        q_rows, kv_rows = rows * branches, T * branches
+        self.attn_traffic = q_rows * (6144 + 3920.5) + kv_rows * 12288
         self.config = {"workload": "multimodal DiT denoising step (CFG pair): 48 blocks x (attention "
                                    "sub-block + GELU FFN sub-block), adaLN-zero, seed 4",
                        "tokens": T, "documents": cu, "hidden": d, "heads": self.cfg.heads,
@@ -449,7 +459,9 @@ def run_ours(args) -> None:
             roof = {"bound": "tensor", "kernel": "h3b::attn::k_fmha (bf16)", "achieved": achieved,
                     "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
                     "peak_source": f"bf16_tflops_sustained of {pk['source']} MEASURED_PEAKS.json",
-                    "traffic": TRAFFIC_BYTES["k_fmha"], "per_launch_tflop": flops_launch / 1e12,
+                    "traffic": (wl.attn_traffic if wl.name == "dit"
+                                else ATTN_TRAFFIC_PER_TOKEN * wl.cu[-1]),
+                    "per_launch_tflop": flops_launch / 1e12,
                     "launch_ms": statistics.mean(attn_list),
                     "share_of_step": attn_ms / ms}
         else:
