@@ -161,13 +161,19 @@ class DiTWorkload:
         # K|V row of the local branches read once (12288 B)
         q_rows, kv_rows = rows * branches, T * branches
         self.attn_traffic = q_rows * (6144 + 3920.5) + kv_rows * 12288
-        self.config = {"workload": "multimodal DiT denoising step (CFG pair): 48 blocks x (attention "
-                                   "sub-block + GELU FFN sub-block), adaLN-zero, seed 4",
-                       "tokens": T, "documents": cu, "hidden": d, "heads": self.cfg.heads,
-                       "head_dim": self.cfg.head_dim, "ffn": ff, "cfg_batch": 2,
-                       "parallelism": (f"cfg{self.layout.cfg_parallel} x "
-                                       f"tokens{self.layout.token_parallel}"),
-                       "l2": "working set several GB per step > 126 MB L2 (no flush needed)"}
+        self.config = self.describe(world)
+
+    @staticmethod
+    def describe(world: int) -> dict:
+        from h3_engine_b200.dit import DiTConfig
+        from h3_engine_b200.parallel import ParallelLayout
+        cfg, L = DiTConfig(), ParallelLayout.plan(world, 0)
+        return {"workload": "multimodal DiT denoising step (CFG pair): 48 blocks x (attention "
+                            "sub-block + GELU FFN sub-block), adaLN-zero, seed 4",
+                "tokens": cfg.tokens, "documents": cfg.cu_seqlens(), "hidden": cfg.hidden,
+                "heads": cfg.heads, "head_dim": cfg.head_dim, "ffn": cfg.ffn, "cfg_batch": 2,
+                "parallelism": f"cfg{L.cfg_parallel} x tokens{L.token_parallel}",
+                "l2": "working set several GB per step > 126 MB L2 (no flush needed)"}
 
     def set_timers(self, gemm, attn):
         for b in self.model.blocks:
@@ -209,11 +215,15 @@ class FFNWorkload:
         self.step_flops = world * 4.0 * tokens * HIDDEN * FFN
         self.rank_gemm_flops = 4.0 * tokens * HIDDEN * FFN
         self.rank_attn_flops = 0
-        self.config = {"workload": "DiT FFN sub-block (seed 2): RMSNorm -> NVFP4 GEMM up 3072->12288 "
-                                   "(+bias, GELU-tanh) -> NVFP4 re-quant -> NVFP4 GEMM down (+bias) "
-                                   "-> residual", "tokens_per_gpu": tokens, "hidden": HIDDEN,
-                       "ffn": FFN, "parallelism": f"token-sharded x{world}, weights replicated",
-                       "l2": "working set ~1.3 GB per step > 126 MB L2 (no flush needed)"}
+        self.config = self.describe(world, tokens)
+
+    @staticmethod
+    def describe(world: int, tokens: int = FFN_TOKENS) -> dict:
+        return {"workload": "DiT FFN sub-block (seed 2): RMSNorm -> NVFP4 GEMM up 3072->12288 "
+                            "(+bias, GELU-tanh) -> NVFP4 re-quant -> NVFP4 GEMM down (+bias) "
+                            "-> residual", "tokens_per_gpu": tokens, "hidden": HIDDEN,
+                "ffn": FFN, "parallelism": f"token-sharded x{world}, weights replicated",
+                "l2": "working set ~1.3 GB per step > 126 MB L2 (no flush needed)"}
 
     def set_timers(self, gemm, attn):
         self.blk.gemm_events = gemm
@@ -288,10 +298,27 @@ class AttentionWorkload:
 
 
 # ----------------------------------------------------------------------------- CPU
-def cpu_dit_estimate(sample_rows: int) -> dict:
+CPU_SAMPLE_SECONDS = 10.0
+
+
+def _timed_repeat(fn, min_seconds: float) -> tuple[float, int]:
+    """Seconds per call of ``fn`` averaged over as many calls as fill
+    ``min_seconds`` (at least one), after one untimed call."""
+    fn()
+    n, t0 = 0, time.perf_counter()
+    while True:
+        fn()
+        n += 1
+        el = time.perf_counter() - t0
+        if el >= min_seconds:
+            return el / n, n
+
+
+def cpu_dit_estimate(sample_rows: int, min_seconds: float = CPU_SAMPLE_SECONDS) -> dict:
     """Extrapolated CPU time of the DiT step from a sample of query rows: the
     attention half (rows x all keys) and the FFN half of one block on
-    ``sample_rows`` rows, scaled to 2 x T rows x 48 blocks."""
+    ``sample_rows`` rows, repeated for ``min_seconds`` of CPU work, scaled to
+    2 x T rows x 48 blocks."""
     from h3_engine_b200.dit import DiTConfig
     from oracle.cpu_torch import AttnRowsCPU, FFNBlockCPU
 
@@ -307,22 +334,19 @@ def cpu_dit_estimate(sample_rows: int) -> dict:
     pos = torch.randint(0, 50, (sample_rows, 3), generator=g).float()
     from h3_engine_b200.rope import rope_tables
     cos, sin = rope_tables(pos, cfg.rope_dims, cfg.theta)
-    h = attn(x, cos, sin)                       # warm
-    t0 = time.perf_counter()
-    h = attn(x, cos, sin)
-    ffn(h)
-    dt = time.perf_counter() - t0
+    dt, n = _timed_repeat(lambda: ffn(attn(x, cos, sin)), min_seconds)
     step_s = dt * (2 * T / sample_rows) * cfg.blocks
     f = cfg.flops_per_eval()
     flops = 2 * (f["nvfp4"] + f["attention"])
     return {"value": flops / step_s / 1e12, "unit": "TFLOP/s", "cores": torch.get_num_threads(),
             "kind": "port", "s_per_step": step_s,
             "sample": (f"{sample_rows} query rows of one block (attention against all {T} keys "
-                       f"+ FFN), {dt:.2f} s, extrapolated linearly to 2 x {T} rows x "
+                       f"+ FFN) x {n} repeats, {dt * n:.1f} s of CPU work, "
+                       f"{dt:.2f} s per sample, extrapolated linearly to 2 x {T} rows x "
                        f"{cfg.blocks} blocks")}
 
 
-def cpu_ffn_run(sample_tokens: int, steps: int = 1) -> dict:
+def cpu_ffn_run(sample_tokens: int, min_seconds: float = CPU_SAMPLE_SECONDS) -> dict:
     from oracle.cpu_torch import FFNBlockCPU
 
     torch.set_num_threads(os.cpu_count() or 1)
@@ -331,14 +355,11 @@ def cpu_ffn_run(sample_tokens: int, steps: int = 1) -> dict:
     w2 = (torch.randn(HIDDEN, FFN, generator=g) * 0.02).to(torch.bfloat16)
     blk = FFNBlockCPU(w1, torch.zeros(FFN), w2, torch.zeros(HIDDEN), torch.ones(HIDDEN), 1e-6)
     x = torch.randn(sample_tokens, HIDDEN, generator=g).to(torch.bfloat16)
-    blk(x)
-    t0 = time.perf_counter()
-    for _ in range(steps):
-        blk(x)
-    dt = (time.perf_counter() - t0) / steps
+    dt, n = _timed_repeat(lambda: blk(x), min_seconds)
     return {"value": 4.0 * sample_tokens * HIDDEN * FFN / dt / 1e12, "unit": "TFLOP/s",
-            "cores": torch.get_num_threads(), "kind": "port", "s_per_step": dt,
-            "sample": f"{sample_tokens} of {FFN_TOKENS} tokens per step"}
+            "cores": torch.get_num_threads(), "kind": "port", "s_per_step": dt * FFN_TOKENS / sample_tokens,
+            "sample": (f"{sample_tokens} of {FFN_TOKENS} tokens x {n} repeats, "
+                       f"{dt * n:.1f} s of CPU work")}
 
 
 def run_reference(args) -> None:
@@ -351,7 +372,7 @@ def run_reference(args) -> None:
         return
     vals = []
     for _ in range(max(args.steps, 1)):
-        r = cpu_dit_estimate(args.cpu_rows) if args.workload == "dit" else cpu_ffn_run(args.cpu_rows)
+        r = cpu_dit_estimate(args.cpu_rows, args.cpu_seconds) if args.workload == "dit" else cpu_ffn_run(args.cpu_rows, args.cpu_seconds)
         vals.append(r)
     v = statistics.median([r["value"] for r in vals])
     r = vals[-1]
@@ -361,7 +382,9 @@ def run_reference(args) -> None:
         "ms_per_step": statistics.median([x["s_per_step"] for x in vals]) * 1e3,
         "higher_is_better": True, "scaling": "strong" if args.workload == "dit" else "weak",
         "vs_baseline": None, "dtype": "fp32 (NVFP4 operands decoded)",
-        "data": "synthetic", "config": {"workload": args.workload + " (CPU, extrapolated sample)"},
+        "data": "synthetic",
+        "config": (DiTWorkload.describe(args.gpus) if args.workload == "dit"
+                   else FFNWorkload.describe(args.gpus)),
         "cpu_baseline": {"value": v, "unit": "TFLOP/s", "cores": r["cores"], "kind": r["kind"],
                          "sample": r["sample"]},
         "e2e": {"value": v, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
@@ -441,11 +464,13 @@ def run_ours(args) -> None:
     ms, e2e_ms = [float(v) for v in t.tolist()]
 
     extras = {}
+    if world == 1 and wl.name == "dit" and not args.no_extras:
+        extras["cuda_graph"] = graph_step_timing(wl, args.steps)
     if rank == 0 and not args.no_extras:
         extras["library_gemm_torch_scaled_mm"] = library_gemm_reference(dev)
         if world == 1 and args.workload != "attention":
-            cpu = (cpu_dit_estimate(args.cpu_rows) if args.workload == "dit"
-                   else cpu_ffn_run(args.cpu_rows))
+            cpu = (cpu_dit_estimate(args.cpu_rows, args.cpu_seconds) if args.workload == "dit"
+                   else cpu_ffn_run(args.cpu_rows, args.cpu_seconds))
             extras["cpu_baseline"] = {k: cpu[k] for k in ("value", "unit", "cores", "kind", "sample")}
 
     if rank == 0:
@@ -504,6 +529,25 @@ def run_ours(args) -> None:
         dist.destroy_process_group()
 
 
+def graph_step_timing(wl, steps: int) -> dict:
+    """The same denoising step replayed from one CUDA graph (one GPU)."""
+    from h3_engine_b200.dit import GraphedSampler
+    g = GraphedSampler(wl.sampler)
+    x = wl.x
+    for _ in range(2):
+        x = g.step(x, wl.i % wl.sampler.steps)
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for k in range(steps):
+        x = g.step(x, (wl.i + k) % wl.sampler.steps)
+    b.record()
+    torch.cuda.synchronize()
+    ms = a.elapsed_time(b) / steps
+    del g
+    return {"ms_per_step": ms, "value": wl.step_flops / (ms * 1e-3) / 1e12, "unit": "TFLOP/s"}
+
+
 def library_gemm_reference(dev) -> dict | None:
     """torch._scaled_mm (cuBLASLt NVFP4, the reference's GEMM call) on the FFN
     GEMM shapes, for context; not part of the timed step."""
@@ -543,8 +587,10 @@ def main() -> None:
     ap.add_argument("--workload", choices=["dit", "ffn", "attention"], default="dit")
     ap.add_argument("--attn-docs", default="32760,1024",
                     help="document lengths of the attention workload (comma-separated)")
-    ap.add_argument("--cpu-rows", type=int, default=64,
+    ap.add_argument("--cpu-rows", type=int, default=256,
                     help="query rows (dit) / tokens (ffn) of the CPU sample")
+    ap.add_argument("--cpu-seconds", type=float, default=CPU_SAMPLE_SECONDS,
+                    help="CPU work per baseline sample (repeats of the row sample)")
     ap.add_argument("--no-extras", action="store_true",
                     help="skip the library GEMM comparison and the CPU baseline (profiling runs)")
     args = ap.parse_args()

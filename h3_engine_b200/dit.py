@@ -124,6 +124,7 @@ class RandomDiT:
         self.out_gamma = vec(d, 1.0, 0.1)
         self.proj_out = _Linear(w(d, d), vec(d))
         self._rope = None
+        self._sel: dict[tuple[int, ...], torch.Tensor] = {}   # CFG-branch selectors
 
     # ------------------------------------------------------------------ pieces
     def temb(self, timesteps: torch.Tensor) -> torch.Tensor:
@@ -159,7 +160,10 @@ class RandomDiT:
         else:
             cu = cfg.cu_seqlens()
             mod_idx = None
-        sel = torch.tensor(branches, device=x.device)
+        key = tuple(branches)
+        if key not in self._sel:          # cached: no host->device copy inside a step
+            self._sel[key] = torch.tensor(branches, device=x.device)
+        sel = self._sel[key]
         st = torch.nn.functional.silu(temb_pair.float())
         h = x
         buf = [torch.empty_like(x), torch.empty_like(x)]
@@ -192,8 +196,15 @@ class Sampler:
 
     def step(self, x: torch.Tensor, i: int) -> torch.Tensor:
         """One denoising step on this rank's latent rows ``x`` [rows, d]."""
-        m, L = self.model, self.layout
         t = torch.full((1,), float(self.sigmas[i]) * 1000.0, device=x.device)
+        dt = float(self.sigmas[i + 1] - self.sigmas[i])
+        return self.step_at(x, t, dt)
+
+    def step_at(self, x: torch.Tensor, t: torch.Tensor, dt) -> torch.Tensor:
+        """The step at timestep ``t`` (device [1]) with Euler increment ``dt``
+        (a float or a device scalar, so a captured graph can be replayed for
+        every step of the schedule)."""
+        m, L = self.model, self.layout
         temb = m.temb(t).float()                           # [1, d]
         te = torch.cat([temb + m.cond.float(), temb]).to(torch.bfloat16)
         if L.cfg_parallel == 1:
@@ -206,7 +217,6 @@ class Sampler:
             v_c, v_u = (v, other) if L.branch == 0 else (other, v)
         g = m.cfg.guidance
         v = v_u.float() + g * (v_c.float() - v_u.float())
-        dt = float(self.sigmas[i + 1] - self.sigmas[i])
         return (x.float() + dt * v).to(torch.bfloat16)
 
     def latent(self, seed: int = 4) -> torch.Tensor:
@@ -215,3 +225,46 @@ class Sampler:
         g = torch.Generator(device=self.model.device).manual_seed(seed * 1000 + 7)
         x = torch.randn(cfg.tokens, cfg.hidden, generator=g, device=self.model.device)
         return x[self.rows].to(torch.bfloat16).contiguous()
+
+
+class GraphedSampler:
+    """``Sampler.step`` captured once into a CUDA graph and replayed for every
+    step of the schedule (the one-evaluation graph of
+    h3_inference/tests/kprofile.py:151-199).  Static input / output rows and
+    device scalars for the timestep and the Euler increment are refreshed
+    before each replay; the first call runs one eager step to warm every
+    buffer and kernel attribute, then captures.  One GPU (a graph holding
+    NCCL collectives is not built here)."""
+
+    def __init__(self, sampler: Sampler):
+        if sampler.layout.world != 1:
+            raise ValueError("GraphedSampler captures the single-GPU layout")
+        self.sampler = sampler
+        self.graph: torch.cuda.CUDAGraph | None = None
+        self.x_in = self.x_out = self.t = self.dt = None
+
+    def _capture(self, x: torch.Tensor) -> None:
+        s = self.sampler
+        dev = x.device
+        self.x_in = x.clone()
+        self.t = torch.zeros(1, device=dev)
+        self.dt = torch.zeros((), device=dev)
+        side = torch.cuda.Stream(device=dev)
+        side.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(side):
+            s.step_at(self.x_in, self.t, self.dt)          # warm-up on the capture stream
+        torch.cuda.current_stream(dev).wait_stream(side)
+        torch.cuda.synchronize(dev)
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph):
+            self.x_out = s.step_at(self.x_in, self.t, self.dt)
+
+    def step(self, x: torch.Tensor, i: int) -> torch.Tensor:
+        s = self.sampler
+        if self.graph is None:
+            self._capture(x)
+        self.x_in.copy_(x)
+        self.t.fill_(float(s.sigmas[i]) * 1000.0)
+        self.dt.fill_(float(s.sigmas[i + 1] - s.sigmas[i]))
+        self.graph.replay()
+        return self.x_out
