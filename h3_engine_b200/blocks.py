@@ -61,9 +61,25 @@ def _buf(ws: dict, name: str, shape, dtype, dev) -> torch.Tensor:
 
 
 class FFNBlock(_GemmTimer):
+    """FFN half of a DiT block: RMSNorm (+adaLN modulation) -> NVFP4 -> up
+    GEMM with the activation in its epilogue -> re-quantization -> down GEMM
+    (+bias, adaLN gate, residual).  ``act="gelu"``: GELU-tanh with bias (the
+    configuration of this model); ``act="swiglu"``: the reference model's
+    SwiGLU feed-forward (``w1`` the fused [value | gate] projection, 2F rows,
+    no bias; h3_inference/transformer/ops.py:62-81)."""
+
     def __init__(self, w1: torch.Tensor, b1: torch.Tensor | None, w2: torch.Tensor,
                  b2: torch.Tensor | None, gamma: torch.Tensor, eps: float = 1e-6,
-                 workspace: dict | None = None):
+                 workspace: dict | None = None, act: str = "gelu"):
+        if act not in ("gelu", "swiglu"):
+            raise ValueError(f"unknown FFN activation {act!r}")
+        self.act = act
+        if act == "swiglu":
+            if b1 is not None:
+                raise ValueError("the SwiGLU feed-forward carries no up-projection bias")
+            if w1.shape[0] % 256:
+                raise ValueError("SwiGLU up-projection rows (2F) must be a multiple of 256")
+            w1 = w1[ops.swiglu_rows(w1.shape[0] // 2).to(w1.device)]
         self.w1 = NVFP4Weight(w1)
         self.w2 = NVFP4Weight(w2)
         self.b1 = None if b1 is None else b1.to(torch.bfloat16).contiguous()
@@ -71,13 +87,13 @@ class FFNBlock(_GemmTimer):
         self.gamma = gamma.to(torch.bfloat16).contiguous()
         self.eps = float(eps)
         self.hidden = self.w1.in_features
-        self.ffn_dim = self.w1.out_features
+        self.ffn_dim = self.w1.out_features // (2 if act == "swiglu" else 1)
         # blocks that run one after another on one stream may share one pool
         self._ws: dict[tuple, dict] = {} if workspace is None else workspace
         self.gemm_events = None
 
     def flops(self, tokens: int) -> int:
-        return 2 * tokens * self.hidden * self.ffn_dim * 2
+        return 2 * tokens * self.hidden * (self.w1.out_features + self.ffn_dim)
 
     def _workspace(self, T: int, dev: torch.device) -> dict:
         key = ("ffn", T, self.hidden, self.ffn_dim, dev)
@@ -109,8 +125,9 @@ class FFNBlock(_GemmTimer):
                                             mod_idx=mod_idx, ws=ws["norm"], amax_hook=hook)
         ws["amax_u"].zero_()
         ev = self._event()
+        act = ops.ACT_SWIGLU if self.act == "swiglu" else ops.ACT_GELU_TANH
         u = ops.gemm(qh, sfh, gsh, T, self.w1.qdata, self.w1.scale_u8, self.w1.global_scale,
-                     self.ffn_dim, self.hidden, bias=self.b1, act=ops.ACT_GELU_TANH,
+                     self.w1.out_features, self.hidden, bias=self.b1, act=act,
                      out=ws["u"], amax_out=ws["amax_u"])
         self._event(ev)
         if hook is not None:

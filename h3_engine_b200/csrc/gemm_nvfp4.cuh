@@ -91,6 +91,9 @@ __device__ __forceinline__ float gelu_tanh(float v) {
   return 0.5f * v * (1.0f + t);
 }
 
+// SWIGLU: the fused up-projection epilogue (act == H3B_ACT_SWIGLU), a separate
+// instantiation so the other epilogues keep their register allocation.
+template <bool SWIGLU>
 __global__ void __launch_bounds__(THREADS, 1) k_gemm_nvfp4(const __grid_constant__ Args p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -257,7 +260,47 @@ __global__ void __launch_bounds__(THREADS, 1) k_gemm_nvfp4(const __grid_constant
       if (lane == 0) mbar_arrive(smem_u32(acc_empty));
 
       const int n_base = n0 + half * 128;
-      if (n_base < p.N && m0 + qd * 32 < p.M) {   // warp-uniform: this warp's box has rows
+      if (SWIGLU) {
+       if (m0 + qd * 32 < p.M) {
+        // this warp's 128 accumulator columns are [value 64 | gate 64] of
+        // output columns n0/2 + 64*half ..; one 64-column chunk out
+        const int row = m0 + qd * 32 + lane;
+        const bool row_ok = row < p.M;
+        const float alpha = gsa * (p.gs_b ? __ldg(p.gs_b) : 1.f);
+        if (lane == 0) bulk_wait_read0();
+        __syncwarp();
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          uint32_t o[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            float r[2];
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+              const float v = __bfloat162float(
+                  __float2bfloat16_rn(__uint_as_float(acc[j * 8 + 2 * e + h]) * alpha));
+              const float g = __bfloat162float(
+                  __float2bfloat16_rn(__uint_as_float(acc[64 + j * 8 + 2 * e + h]) * alpha));
+              const float sg = __bfloat162float(__float2bfloat16_rn(g / (1.0f + __expf(-g))));
+              r[h] = v * sg;
+            }
+            o[e] = pack_bf16x2(r[0], r[1]);
+            if (row_ok) {
+              amax = fmaxf(amax, fabsf(__uint_as_float(o[e] << 16)));
+              amax = fmaxf(amax, fabsf(__uint_as_float(o[e] & 0xFFFF0000u)));
+            }
+          }
+          *reinterpret_cast<uint4*>(stage + lane * 128 + ((j ^ (lane & 7)) << 4)) =
+              make_uint4(o[0], o[1], o[2], o[3]);
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          tma_store_2d(&p.tmap_d, stage_s, (n0 >> 1) + half * 64, m0 + qd * 32);
+          bulk_commit();
+        }
+       }
+      } else if (n_base < p.N && m0 + qd * 32 < p.M) {   // warp-uniform: this warp's box has rows
         const int row = m0 + qd * 32 + lane;
         const bool row_ok = row < p.M;
         const float alpha =

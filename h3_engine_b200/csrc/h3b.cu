@@ -219,9 +219,13 @@ int h3b_nvfp4_gemm(const void* A, const void* sfA, const float* gsA, int64_t M, 
   if (gate_idx && !gate) return H3B_ERR_INVALID_ARG;
   if (gsb_seg < 0 || (gsb_seg && (gsb_seg % 128 || N % gsb_seg))) return H3B_ERR_INVALID_ARG;
   if (K % gemm::KB_ELEMS || N % 128 || a_rows % 128 || a_rows < M) return H3B_ERR_INVALID_ARG;
-  if (ldd < N || ldd % 8) return H3B_ERR_INVALID_ARG;
+  if (act != H3B_ACT_NONE && act != H3B_ACT_GELU_TANH && act != H3B_ACT_SWIGLU)
+    return H3B_ERR_INVALID_ARG;
+  const bool swiglu = act == H3B_ACT_SWIGLU;
+  if (swiglu && (N % gemm::BN || bias || residual || gate || gsb_seg)) return H3B_ERR_INVALID_ARG;
+  const int64_t n_out = swiglu ? N / 2 : N;          // columns of D
+  if (ldd < n_out || ldd % 8) return H3B_ERR_INVALID_ARG;
   if (residual && (ldr < N || ldr % 8)) return H3B_ERR_INVALID_ARG;
-  if (act != H3B_ACT_NONE && act != H3B_ACT_GELU_TANH) return H3B_ERR_INVALID_ARG;
   if (M > (int64_t)INT32_MAX - 256 || N > (int64_t)INT32_MAX || K > (int64_t)INT32_MAX)
     return H3B_ERR_INVALID_ARG;
   if (M == 0) return H3B_OK;
@@ -236,9 +240,13 @@ int h3b_nvfp4_gemm(const void* A, const void* sfA, const float* gsA, int64_t M, 
   static std::once_flag attr_once;
   static cudaError_t attr_err = cudaSuccess;
   std::call_once(attr_once, [] {
-    attr_err = cudaFuncSetAttribute(gemm::k_gemm_nvfp4,
+    attr_err = cudaFuncSetAttribute(gemm::k_gemm_nvfp4<false>,
                                     cudaFuncAttributeMaxDynamicSharedMemorySize,
                                     gemm::SMEM_BYTES);
+    if (attr_err == cudaSuccess)
+      attr_err = cudaFuncSetAttribute(gemm::k_gemm_nvfp4<true>,
+                                      cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      gemm::SMEM_BYTES);
   });
   if (attr_err != cudaSuccess) return H3B_ERR_CUDA;
 
@@ -250,7 +258,7 @@ int h3b_nvfp4_gemm(const void* A, const void* sfA, const float* gsA, int64_t M, 
   rc = make_tmap_u8_sw128(&args.tmap_b, B, (uint64_t)N, (uint64_t)(K / 2), (uint64_t)(K / 2),
                           gemm::KB_BYTES, gemm::BN);
   if (rc != H3B_OK) return rc;
-  rc = make_tmap_bf16_sw128(&args.tmap_d, D, (uint64_t)M, (uint64_t)N, (uint64_t)ldd,
+  rc = make_tmap_bf16_sw128(&args.tmap_d, D, (uint64_t)M, (uint64_t)n_out, (uint64_t)ldd,
                             gemm::OUT_CHUNK_COLS, 32);
   if (rc != H3B_OK) return rc;
   args.sfa = static_cast<const uint8_t*>(sfA);
@@ -274,8 +282,12 @@ int h3b_nvfp4_gemm(const void* A, const void* sfA, const float* gsA, int64_t M, 
   if (num_tiles > INT32_MAX) return H3B_ERR_INVALID_ARG;
   args.num_tiles = (int)num_tiles;
   const int grid = (int)std::min<int64_t>(num_tiles, num_sms());
-  gemm::k_gemm_nvfp4<<<grid, gemm::THREADS, gemm::SMEM_BYTES, static_cast<cudaStream_t>(stream)>>>(
-      args);
+  if (swiglu)
+    gemm::k_gemm_nvfp4<true><<<grid, gemm::THREADS, gemm::SMEM_BYTES,
+                               static_cast<cudaStream_t>(stream)>>>(args);
+  else
+    gemm::k_gemm_nvfp4<false><<<grid, gemm::THREADS, gemm::SMEM_BYTES,
+                                static_cast<cudaStream_t>(stream)>>>(args);
   return launched(cudaGetLastError());
 }
 

@@ -15,6 +15,26 @@ SF_ROWMAJOR = 0
 SF_SWIZZLED = 1
 ACT_NONE = 0
 ACT_GELU_TANH = 1
+ACT_SWIGLU = 2
+
+
+def swiglu_rows(ffn_dim: int) -> torch.Tensor:
+    """Row order of a fused SwiGLU up-projection weight ([value | gate], 2F
+    rows, the reference's chunk order) that the ACT_SWIGLU epilogue reads:
+    per 256 rows, value f..f+63, gate f..f+63, value f+64..f+127, gate
+    f+64..f+127 (f = 128 t), so one epilogue warp holds a value column and its
+    gate.  ``w[swiglu_rows(F)]`` permutes rows; NVFP4 block scales are per row
+    and the global scale is the whole tensor's, so quantizing the permuted
+    weight gives the permuted rows of the quantized weight."""
+    if ffn_dim % 128:
+        raise ValueError("SwiGLU ffn_dim must be a multiple of 128")
+    idx = []
+    for t in range(ffn_dim // 128):
+        for half in range(2):
+            base = 128 * t + 64 * half
+            idx.extend(range(base, base + 64))
+            idx.extend(range(ffn_dim + base, ffn_dim + base + 64))
+    return torch.tensor(idx, dtype=torch.long)
 M_ALIGN = 128
 
 
@@ -122,7 +142,8 @@ def gemm(qa: torch.Tensor, sfa: torch.Tensor, gsa: torch.Tensor | None, M: int,
          residual: torch.Tensor | None = None, act: int = ACT_NONE,
          gate: torch.Tensor | None = None, gate_idx: torch.Tensor | None = None,
          out: torch.Tensor | None = None, amax_out: torch.Tensor | None = None) -> torch.Tensor:
-    """``out[M, N] = epilogue(gsa*gsb * deq(qa) @ deq(qb)^T)`` in bf16.
+    """``out[M, N] = epilogue(gsa*gsb * deq(qa) @ deq(qb)^T)`` in bf16
+    (``out[M, N/2]`` for ``act=ACT_SWIGLU`` with ``qb`` in ``swiglu_rows`` order).
 
     ``qa``: u8 ``[a_rows, K/2]`` (a_rows % 128 == 0) with swizzled ``sfa``;
     ``qb``: u8 ``[N, K/2]`` with swizzled ``sfb``.  ``amax_out`` (fp32 [1],
@@ -132,8 +153,11 @@ def gemm(qa: torch.Tensor, sfa: torch.Tensor, gsa: torch.Tensor | None, M: int,
     if qa.dtype != torch.uint8 or qb.dtype != torch.uint8:
         raise TypeError("packed operands must be uint8")
     a_rows = qa.shape[0]
+    n_out = N // 2 if act == ACT_SWIGLU else N
+    if act == ACT_SWIGLU and (bias is not None or residual is not None or gate is not None):
+        raise ValueError("the SwiGLU epilogue takes no bias, residual or gate")
     if out is None:
-        out = torch.empty(M, N, dtype=torch.bfloat16, device=dev)
+        out = torch.empty(M, n_out, dtype=torch.bfloat16, device=dev)
     if bias is not None and (bias.dtype != torch.bfloat16 or bias.numel() != N):
         raise ValueError("bias must be bf16 [N]")
     if residual is not None and (residual.dtype != torch.bfloat16 or residual.stride(-1) != 1):

@@ -43,7 +43,7 @@ enum { H3B_SF_ROWMAJOR = 0,  /* e4m3 [rows, K/16], row-major                    
 };
 
 /* GEMM epilogue activations. */
-enum { H3B_ACT_NONE = 0, H3B_ACT_GELU_TANH = 1 };
+enum { H3B_ACT_NONE = 0, H3B_ACT_GELU_TANH = 1, H3B_ACT_SWIGLU = 2 };
 
 /* ------------------------------------------------------------------ library */
 H3B_API int h3b_version(void);
@@ -104,7 +104,15 @@ H3B_API int h3b_nvfp4_dequantize(const void* q, const void* sf, int sf_layout, i
  *   h3_inference/kernels/elementwise_norm_rope.py:150-163);
  *   v += residual[m, n] (bf16, row stride ldr, optional);
  *   D = bf16(v); amax_out (optional) is atomically max-reduced with |D|
- *   (the caller zeroes it first).                                            */
+ *   (the caller zeroes it first).
+ * act == H3B_ACT_SWIGLU: the fused up-projection of a SwiGLU feed-forward
+ *   (h3_inference/kernels/ffn_qkvo_gemms.py:31-35, transformer/ops.py:62-73:
+ *   value, gate = proj(x).chunk(2); value * silu(gate)).  B holds the 2F rows
+ *   [value | gate] interleaved in 64-row blocks -- per 256 rows: value
+ *   f..f+63, gate f..f+63, value f+64..f+127, gate f+64..f+127 (f = 128 t) --
+ *   and D is [M, N/2]: D = bf16(bf16(v) * bf16(silu(bf16(g)))), the rounding
+ *   of the reference's bf16 ops.  N % 256 == 0; bias, gate and residual must
+ *   be NULL.                                                                 */
 H3B_API int h3b_nvfp4_gemm(const void* A, const void* sfA, const float* gsA, int64_t M, int64_t a_rows,
                    const void* B, const void* sfB, const float* gsB, int64_t gsb_seg, int64_t N,
                    int64_t K, const void* bias, const void* residual, int64_t ldr,

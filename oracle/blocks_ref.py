@@ -171,3 +171,32 @@ def ffn_block_mod(x, gamma, eps, w1q, b1, w2q, b2, shift=None, scale=None, gate=
         y = y * R.bf16_round(gate).astype(np.float64)[idx]
     y = y + x.astype(np.float64)
     return R.bf16_round(y.astype(np.float32))
+
+
+def silu_bf16(g):
+    """silu of bf16 values computed in fp32 and rounded to bf16 (torch's bf16
+    ``F.silu``), h3_inference/transformer/ops.py:62-73."""
+    g = np.asarray(g, dtype=np.float32)
+    return R.bf16_round((g / (np.float32(1.0) + np.exp(-g))).astype(np.float32))
+
+
+def swiglu_ffn_block_mod(x, gamma, eps, wupq, wdownq, shift=None, scale=None, gate=None,
+                         mod_idx=None):
+    """FFN half of the reference-shape block: RMSNorm (+modulation) -> NVFP4
+    up-projection to [value | gate] (2F, no bias) -> value * silu(gate), each
+    op rounded to bf16 as the reference's bf16 modules do
+    (h3_inference/kernels/ffn_qkvo_gemms.py:31-35) -> NVFP4 down-projection
+    (no bias) -> adaLN gate and residual.  ``wupq`` is the (q, sf, gs) triple
+    of the [2F, d] weight in the reference's [value | gate] row order."""
+    x = R.bf16_round(x)
+    h = rmsnorm(x, gamma, eps, shift, scale, mod_idx)
+    u2, _ = nvfp4_linear_from_bf16(h, *wupq)
+    F = u2.shape[1] // 2
+    u = R.bf16_round((u2[:, :F] * silu_bf16(u2[:, F:])).astype(np.float32))
+    qa, sa, ga = R.quantize(u)
+    y = R.gemm_ref(qa, sa, ga, *wdownq, M=x.shape[0], N=wdownq[0].shape[0])
+    if gate is not None:
+        idx = np.zeros(x.shape[0], dtype=np.int64) if mod_idx is None else np.asarray(mod_idx)
+        y = y * R.bf16_round(gate).astype(np.float64)[idx]
+    y = y + x.astype(np.float64)
+    return R.bf16_round(y.astype(np.float32)), u

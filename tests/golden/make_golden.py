@@ -16,6 +16,11 @@ modified).  What comes from where:
   (``h3_inference/kernels/elementwise_norm_rope.py:25-40,104-122``),
   ``H3RotaryPosEmbed`` (``h3_inference/transformer/model.py:23-38``) and
   ``packed_self_attention`` (SDPA path, ``h3_inference/kernels/packed_self_attn.py:31-37``).
+* ``refblock_golden.npz`` -- one ``H3TransformerBlock`` of the reference model
+  (``h3_inference/transformer/model.py:157-209``: RMSNorm + gather-modulate,
+  attention with qk-norm and 16/16/16 RoPE, gated residual, SwiGLU
+  feed-forward) run in bf16 on CPU through its stock paths, at small shapes
+  (hidden 256, 2 heads x 128, ffn 256, 128 tokens, three modality tables).
 """
 from __future__ import annotations
 
@@ -163,6 +168,48 @@ def block_cases(ref_root: Path) -> dict[str, np.ndarray]:
     return out
 
 
+def ref_block_case(ref_root: Path) -> dict[str, np.ndarray]:
+    sys.path.insert(0, str(ref_root))
+    from h3_inference.transformer.model import H3RotaryPosEmbed, H3TransformerBlock
+
+    C, H, D, F, T = 256, 2, 128, 256, 128
+    g = _rng(21)
+    blk = H3TransformerBlock(C, H, D, F, time_embed_dim=64, norm_eps=1e-5, qk_norm_eps=1e-5)
+    blk = blk.to(torch.bfloat16).eval()
+    with torch.no_grad():
+        for name, p in blk.named_parameters():
+            if name.endswith("norm1.weight") or name.endswith("norm2.weight") or "norm_q" in name \
+                    or "norm_k" in name:
+                p.copy_(1 + 0.1 * torch.randn(p.shape, generator=g))
+            elif p.dim() == 2:
+                p.copy_(torch.randn(p.shape, generator=g) / p.shape[1] ** 0.5)
+            else:
+                p.copy_(0.01 * torch.randn(p.shape, generator=g))
+        tables = [0.1 * torch.randn(3, C, generator=g) for _ in range(2)]
+        tables.append(0.5 + 0.2 * torch.randn(3, C, generator=g))           # gate_msa
+        tables += [0.1 * torch.randn(3, C, generator=g) for _ in range(2)]
+        tables.append(0.5 + 0.2 * torch.randn(3, C, generator=g))           # gate_mlp
+        tables = [t.to(torch.bfloat16) for t in tables]
+        blk.folded_modulation = tuple(tables)
+        x = torch.randn(1, T, C, generator=g).to(torch.bfloat16)
+        idx = torch.cat([torch.zeros(96), torch.ones(16), 2 * torch.ones(16)]).long()
+        pos = torch.stack([torch.arange(T) // 32, (torch.arange(T) // 8) % 4,
+                           torch.arange(T) % 8], dim=1).float()
+        cos, sin = H3RotaryPosEmbed(rope_freq_dim=16, rope_theta=10000.0)(pos)
+        y = blk(x, None, idx, (cos, sin))
+    out = {"x_bits": R.bf16_bits(x.float().numpy()), "y_bits": R.bf16_bits(y.float().numpy()),
+           "idx": idx.numpy(), "pos": pos.numpy(), "cos": cos.numpy(), "sin": sin.numpy(),
+           "eps": np.array([1e-5], dtype=np.float32)}
+    names = ["shift_msa", "scale_msa", "gate_msa", "shift_mlp", "scale_mlp", "gate_mlp"]
+    for n, t in zip(names, tables):
+        out[n + "_bits"] = R.bf16_bits(t.float().numpy())
+    for name, p in blk.named_parameters():
+        if name.startswith("adaln_proj"):
+            continue
+        out["w." + name + "_bits"] = R.bf16_bits(p.detach().float().numpy())
+    return out
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default="/root/reference")
@@ -170,7 +217,9 @@ def main() -> None:
     ref_root = Path(args.reference)
     np.savez_compressed(HERE / "nvfp4_golden.npz", **nvfp4_cases(ref_root))
     np.savez_compressed(HERE / "blocks_golden.npz", **block_cases(ref_root))
-    print("wrote", HERE / "nvfp4_golden.npz", HERE / "blocks_golden.npz")
+    np.savez_compressed(HERE / "refblock_golden.npz", **ref_block_case(ref_root))
+    print("wrote", HERE / "nvfp4_golden.npz", HERE / "blocks_golden.npz",
+          HERE / "refblock_golden.npz")
 
 
 if __name__ == "__main__":
