@@ -1,7 +1,7 @@
 """Benchmark of the NVFP4 DiT hot path on B200.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl h3b|reference]
-                    [--workload dit|ffn|attention] [--attn-docs 32760,1024]
+                    [--workload dit|ffn|attention|refblock|quant] [--attn-docs 32760,1024]
 
 Default workload ("dit"): one denoising step of the full multimodal DiT --
 48 blocks (hidden 3072, 24 heads x 128, FFN 12288 GELU/bias, adaLN-zero),
@@ -22,6 +22,14 @@ e2e         = the same metric through Sampler.step with the step's latent rows
 
 "ffn": the DiT FFN sub-block on 32768 tokens x 3072 (FFN 12288), one
 independent shard per GPU (weak scaling, no collective).
+
+"quant": the quantize/pack microbenchmark (amax + NVFP4 quantization of bf16
+[M, K], M in {4096, 32768}, K in {3072, 12288}, 0.1 % outliers), GB/s against
+the HBM roofline.
+
+"refblock": one transformer block at the reference model's own shapes
+(hidden 5376, 56 heads x 128, SwiGLU ffn 14336, 38247 tokens, one document),
+one replica per GPU.
 
 "attention": the packed varlen attention kernel alone (24 heads x 128, bf16,
 documents of --attn-docs tokens, default the DiT packing 32760 + 1024) on a
@@ -297,6 +305,160 @@ class AttentionWorkload:
         self.y_h.copy_(self.out, non_blocking=True)
 
 
+class RefBlockWorkload:
+    """One transformer block at the reference model's own shapes
+    (h3_inference/transformer/model.py:211-230: hidden 5376, 56 heads x 128,
+    SwiGLU ffn 14336, eps 1e-5, 16/16/16 RoPE, three modality tables) on the
+    38247-token sequence of its production cell, one document, random-init
+    weights (seed 5)."""
+    name = "refblock"
+    C, H, D, F, TOKENS = 5376, 56, 128, 14336, 38247
+
+    def __init__(self, dev, world: int, rank: int):
+        from h3_engine_b200.blocks import AttnBlock, DiTBlock, FFNBlock
+        from h3_engine_b200.rope import reference_dims, rope_tables
+        C, H, D, F, T = self.C, self.H, self.D, self.F, self.TOKENS
+        HD = H * D
+        g = torch.Generator(device=dev).manual_seed(5 + 1000 * rank)
+
+        def w(n, k):
+            return (torch.randn(n, k, generator=g, device=dev) / k ** 0.5).to(torch.bfloat16)
+
+        def vec(n, mean, std):
+            return (mean + std * torch.randn(n, generator=g, device=dev)).to(torch.bfloat16)
+
+        self.ws: dict = {}
+        attn = AttnBlock(w(HD, C), w(HD, C), w(HD, C), w(C, HD), vec(C, 1.0, 0.1),
+                         vec(D, 1.0, 0.1), vec(D, 1.0, 0.1), heads=H, eps=1e-5, qk_eps=1e-5,
+                         workspace=self.ws)
+        ffn = FFNBlock(w(2 * F, C), None, w(C, F), None, vec(C, 1.0, 0.1), eps=1e-5,
+                       workspace=self.ws, act="swiglu")
+        self.blk = DiTBlock(attn, ffn)
+        self.mod = tuple(((0.5 if j in (2, 5) else 0.0)
+                          + 0.1 * torch.randn(3, C, generator=g, device=dev)).to(torch.bfloat16)
+                         for j in range(6))
+        n_vid = T - 2048
+        self.idx = torch.cat([torch.zeros(n_vid), torch.ones(1024), 2 * torch.ones(1024)]).to(
+            torch.int32).to(dev)
+        pos = torch.stack([torch.arange(T) // 1024, (torch.arange(T) // 32) % 32,
+                           torch.arange(T) % 32], dim=1).float().to(dev)
+        self.rope = rope_tables(pos, reference_dims(16), 10000.0)
+        self.x = torch.randn(T, C, generator=g, device=dev).to(torch.bfloat16)
+        self.y = torch.empty_like(self.x)
+        self.rank_gemm_flops = 2 * T * C * 3 * HD + 2 * T * HD * C + 2 * T * C * 2 * F + 2 * T * F * C
+        self.rank_attn_flops = 4 * HD * T * T
+        self.step_flops = world * (self.rank_gemm_flops + self.rank_attn_flops)
+        self.attn_traffic = T * (3 * HD * 2 + HD * 2)    # q|k|v read once, O written
+        self.config = self.describe(world)
+
+    @classmethod
+    def describe(cls, world: int) -> dict:
+        return {"workload": "one H3TransformerBlock at the reference model's shapes: RMSNorm + "
+                            "gather-modulate, NVFP4 QKV (56 x 128 heads), qk-norm + 16/16/16 RoPE, "
+                            "attention over the whole sequence, gated residual, SwiGLU FFN 14336",
+                "tokens": cls.TOKENS, "hidden": cls.C, "heads": cls.H, "head_dim": cls.D,
+                "ffn": cls.F, "parallelism": f"replicas x{world}",
+                "l2": "working set several GB per step > 126 MB L2 (no flush needed)"}
+
+    def set_timers(self, gemm, attn):
+        self.blk.attn.gemm_events = self.blk.ffn.gemm_events = gemm
+        self.blk.attn.attn_events = attn
+
+    def step(self):
+        self.blk(self.x, self.rope, [0, self.TOKENS], self.mod, self.idx, out=self.y)
+
+    def e2e_setup(self):
+        self.x_h = self.x.cpu().pin_memory()
+        self.y_h = torch.empty_like(self.x_h).pin_memory()
+        self.x_d = torch.empty_like(self.x)
+        return self.x_h.numel() * 2, self.y_h.numel() * 2
+
+    def e2e_step(self):
+        self.x_d.copy_(self.x_h, non_blocking=True)
+        self.blk(self.x_d, self.rope, [0, self.TOKENS], self.mod, self.idx, out=self.y)
+        self.y_h.copy_(self.y, non_blocking=True)
+
+
+class QuantWorkload:
+    """The quantize / pack microbenchmark: amax + NVFP4 quantization (codes,
+    blocked e4m3 scales, fp32 global scale) of bf16 [M, K] for M in {4096,
+    32768} and K in {3072, 12288}, values N(0, 1) with 0.1 % of entries x50
+    (seed 1).  Algorithmic bytes 4.5625 per element: the amax read (2 B), the
+    quantization read (2 B), codes (0.5 B) and scales (0.0625 B)."""
+    name = "quant"
+    SHAPES = ((4096, 3072), (4096, 12288), (32768, 3072), (32768, 12288))
+
+    def __init__(self, dev, world: int, rank: int):
+        from h3_engine_b200 import ops
+        self.ops = ops
+        g = torch.Generator(device=dev).manual_seed(1 + 1000 * rank)
+        self.xs, self.outs = [], []
+        for M, K in self.SHAPES:
+            x = torch.randn(M, K, generator=g, device=dev)
+            hot = torch.rand(M, K, generator=g, device=dev) < 1e-3
+            x = torch.where(hot, x * 50, x).to(torch.bfloat16)
+            self.xs.append(x)
+            self.outs.append((torch.empty(M, K // 2, dtype=torch.uint8, device=dev),
+                              torch.empty(M * K // 16, dtype=torch.uint8, device=dev),
+                              torch.zeros(1, device=dev), torch.empty(1, device=dev)))
+        elems = sum(M * K for M, K in self.SHAPES)
+        self.bytes_per_step = 4.5625 * elems
+        self.quant_bytes = 2.5625 * elems            # the quantization kernel alone
+        self.step_bytes = world * self.bytes_per_step
+        self.rank_gemm_flops = self.rank_attn_flops = 0
+        self.events = None
+        self.config = self.describe(world)
+
+    @classmethod
+    def describe(cls, world: int) -> dict:
+        return {"workload": "NVFP4 quantize/pack (amax + codes + blocked e4m3 scales + fp32 "
+                            "global scale), N(0,1) with 0.1% outliers x50, seed 1",
+                "shapes": [list(s) for s in cls.SHAPES], "parallelism": f"replicas x{world}",
+                "l2": "1.1 GB of inputs per step > 126 MB L2 (no flush needed)"}
+
+    def set_timers(self, gemm, attn):
+        self.events = attn
+
+    def _run(self, xs):
+        ops = self.ops
+        for x, (q, sf, amax, gs) in zip(xs, self.outs):
+            amax.zero_()
+            ops.amax(x, out=amax)
+            if self.events is not None:
+                a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                a.record()
+            ops.quantize(x, mpad=x.shape[0], amax_t=amax, q_out=q, sf_out=sf, gs_out=gs)
+            if self.events is not None:
+                b.record()
+                self.events.append((a, b))
+
+    def step(self):
+        self._run(self.xs)
+
+    def roofline(self, pk, steps, ms, kernel_ms):
+        achieved = self.quant_bytes * steps / (kernel_ms * 1e-3) / 1e9
+        return {"bound": "hbm", "kernel": "h3b::k_nvfp4_quantize<swizzled>", "achieved": achieved,
+                "peak": pk["hbm"], "unit": "GB/s", "frac": achieved / pk["hbm"],
+                "peak_source": f"hbm_gbs of {pk['source']} MEASURED_PEAKS.json",
+                "traffic": None, "algorithmic_bytes_per_step": self.quant_bytes,
+                "whole_step_gbs": self.bytes_per_step / (ms * 1e-3) / 1e9,
+                "whole_step_frac": self.bytes_per_step / (ms * 1e-3) / 1e9 / pk["hbm"]}
+
+    def e2e_setup(self):
+        self.x_h = [x.cpu().pin_memory() for x in self.xs]
+        self.x_d = [torch.empty_like(x) for x in self.xs]
+        self.q_h = [torch.empty_like(o[0], device="cpu").pin_memory() for o in self.outs]
+        return (sum(x.numel() * 2 for x in self.xs),
+                sum(o[0].numel() + o[1].numel() + 4 for o in self.outs))
+
+    def e2e_step(self):
+        for xh, xd in zip(self.x_h, self.x_d):
+            xd.copy_(xh, non_blocking=True)
+        self._run(self.x_d)
+        for qh, o in zip(self.q_h, self.outs):
+            qh.copy_(o[0], non_blocking=True)
+
+
 # ----------------------------------------------------------------------------- CPU
 CPU_SAMPLE_SECONDS = 10.0
 
@@ -366,8 +528,8 @@ def run_reference(args) -> None:
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
-    if args.workload == "attention":
-        print(json.dumps({"impl": "reference", "unavailable": "the attention-only profiling "
+    if args.workload in ("attention", "refblock", "quant"):
+        print(json.dumps({"impl": "reference", "unavailable": f"the {args.workload} profiling "
                           "workload has no CPU arm; the dit and ffn workloads have one"}), flush=True)
         return
     vals = []
@@ -411,6 +573,10 @@ def run_ours(args) -> None:
         wl = DiTWorkload(dev, world, rank)
     elif args.workload == "ffn":
         wl = FFNWorkload(dev, world, rank)
+    elif args.workload == "refblock":
+        wl = RefBlockWorkload(dev, world, rank)
+    elif args.workload == "quant":
+        wl = QuantWorkload(dev, world, rank)
     else:
         wl = AttentionWorkload(dev, world, rank, [int(n) for n in args.attn_docs.split(",")])
     for _ in range(args.warmup):
@@ -468,7 +634,7 @@ def run_ours(args) -> None:
         extras["cuda_graph"] = graph_step_timing(wl, args.steps)
     if rank == 0 and not args.no_extras:
         extras["library_gemm_torch_scaled_mm"] = library_gemm_reference(dev)
-        if world == 1 and args.workload != "attention":
+        if world == 1 and args.workload in ("dit", "ffn"):
             cpu = (cpu_dit_estimate(args.cpu_rows, args.cpu_seconds) if args.workload == "dit"
                    else cpu_ffn_run(args.cpu_rows, args.cpu_seconds))
             extras["cpu_baseline"] = {k: cpu[k] for k in ("value", "unit", "cores", "kind", "sample")}
@@ -476,7 +642,9 @@ def run_ours(args) -> None:
     if rank == 0:
         pk = peaks()
         gemm_tflops = wl.rank_gemm_flops / (gemm_ms * 1e-3) / 1e12 if gemm_ms else None
-        if attn_list:
+        if hasattr(wl, "roofline"):
+            roof = wl.roofline(pk, args.steps, ms, sum(attn_list))
+        elif attn_list:
             n_launch = len(attn_list)
             flops_launch = wl.rank_attn_flops * args.steps / n_launch
             achieved = flops_launch / (statistics.mean(attn_list) * 1e-3) / 1e12
@@ -484,7 +652,7 @@ def run_ours(args) -> None:
             roof = {"bound": "tensor", "kernel": "h3b::attn::k_fmha (bf16)", "achieved": achieved,
                     "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
                     "peak_source": f"bf16_tflops_sustained of {pk['source']} MEASURED_PEAKS.json",
-                    "traffic": (wl.attn_traffic if wl.name == "dit"
+                    "traffic": (wl.attn_traffic if wl.name in ("dit", "refblock")
                                 else ATTN_TRAFFIC_PER_TOKEN * wl.cu[-1]),
                     "per_launch_tflop": flops_launch / 1e12,
                     "launch_ms": statistics.mean(attn_list),
@@ -500,18 +668,24 @@ def run_ours(args) -> None:
                                    "MEASURED_PEAKS.json (dense FP4 = 4x bf16 on B200)",
                     "traffic": TRAFFIC_BYTES["k_gemm_nvfp4"],
                     "per_launch_tflop": flops_launch / 1e12, "share_of_step": gemm_ms / ms}
+        if hasattr(wl, "step_bytes"):           # memory-bound workload: GB/s
+            unit, work, scale = "GB/s", wl.step_bytes, 1e9
+            dtype = "bf16 in, e2m1 codes + e4m3 scales + fp32 global scale out"
+        else:
+            unit, work, scale = "TFLOP/s", wl.step_flops, 1e12
+            dtype = "nvfp4 GEMMs (e2m1 x e4m3/16 x fp32 scale, fp32 accumulate) + bf16 attention"
         line = {
             "metric": METRIC,
-            "value": wl.step_flops / (ms * 1e-3) / 1e12,
-            "unit": "TFLOP/s",
+            "value": work / (ms * 1e-3) / scale,
+            "unit": unit,
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": ms, "higher_is_better": True,
             "scaling": "strong" if wl.name == "dit" else "weak",
             "vs_baseline": None,
-            "dtype": "nvfp4 GEMMs (e2m1 x e4m3/16 x fp32 scale, fp32 accumulate) + bf16 attention",
+            "dtype": dtype,
             "data": "synthetic (seeded random-init weights and latent of the configured shapes)",
             "config": wl.config,
-            "e2e": {"value": wl.step_flops / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s",
+            "e2e": {"value": work / (e2e_ms * 1e-3) / scale, "unit": unit,
                     "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
             "roofline": roof,
             "nvfp4_gemm_tflops_per_gpu": gemm_tflops,
@@ -584,7 +758,8 @@ def main() -> None:
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["h3b", "reference"], default="h3b")
-    ap.add_argument("--workload", choices=["dit", "ffn", "attention"], default="dit")
+    ap.add_argument("--workload", choices=["dit", "ffn", "attention", "refblock", "quant"],
+                    default="dit")
     ap.add_argument("--attn-docs", default="32760,1024",
                     help="document lengths of the attention workload (comma-separated)")
     ap.add_argument("--cpu-rows", type=int, default=256,

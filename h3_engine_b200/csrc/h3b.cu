@@ -167,10 +167,9 @@ int h3b_nvfp4_quantize(const void* x, int64_t M, int64_t K, int64_t ldx, const f
   if (!amax && !(gs_in > 0.f)) return H3B_ERR_INVALID_ARG;
   if (!q || !sf || (M > 0 && !x)) return H3B_ERR_INVALID_ARG;
   if ((M > 0 && !aligned16(x)) || (reinterpret_cast<uintptr_t>(q) & 3u)) return H3B_ERR_ALIGNMENT;
-  const int64_t total = Mpad * (K / 8);
-  if (total == 0) return H3B_OK;
-  const int64_t per_block = (int64_t)kQuantThreads * kQuantUnroll;
-  int64_t blocks = (total + per_block - 1) / per_block;
+  if (Mpad == 0) return H3B_OK;
+  constexpr int64_t rows_per_block = kQuantThreads / 32;      // one warp per row
+  int64_t blocks = (Mpad + rows_per_block - 1) / rows_per_block;
   const int64_t cap = (int64_t)num_sms() * 8;
   if (blocks > cap) blocks = cap;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
@@ -353,9 +352,12 @@ int h3b_qk_norm_rope(void* q, int64_t q_stride, int64_t q_off, void* k, int64_t 
                      float eps, const float* cos, const float* sin, int R, int64_t cs_stride,
                      void* stream) {
   if (T < 0 || H <= 0 || (D != 64 && D != 128)) return H3B_ERR_INVALID_ARG;
-  const int epl = D / 32;
   if (cos != nullptr) {
-    if (!sin || R <= 0 || R > D || R % 2 || (R / 2) % epl || cs_stride < R) return H3B_ERR_INVALID_ARG;
+    // the partner of a lane's 8 columns is a whole lane away: R/2 % 8 == 0;
+    // rows of the tables are read as float4: 16-byte aligned
+    if (!sin || R <= 0 || R > D || (R / 2) % 8 || cs_stride < R || cs_stride % 4)
+      return H3B_ERR_INVALID_ARG;
+    if (!aligned16(cos) || !aligned16(sin)) return H3B_ERR_ALIGNMENT;
   } else {
     R = 0;
   }
@@ -382,9 +384,8 @@ int h3b_qk_norm_rope(void* q, int64_t q_stride, int64_t q_off, void* k, int64_t 
   a.sin = sin;
   a.cs_stride = cs_stride;
   a.eps = eps;
-  const int64_t items = T * 2 * H;
-  int64_t blocks = (items + kRopeWarps - 1) / kRopeWarps;
-  const int64_t cap = (int64_t)num_sms() * 16;
+  int64_t blocks = (T + kRopeWarps - 1) / kRopeWarps;     // one warp per row
+  const int64_t cap = (int64_t)num_sms() * 8;
   if (blocks > cap) blocks = cap;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (D == 128)

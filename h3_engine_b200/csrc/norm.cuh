@@ -32,6 +32,9 @@ struct NormArgs {
 constexpr int kNormWarps = 8;   // rows per CTA, one warp per row
 constexpr int kNormCacheChunks = 12;   // rows of K <= 3072 stay in registers
 
+// y[0..8) of row `row`, columns chunk*256 + lane*8 ..: (x * rstd) * gamma,
+// then * (1 + scale) + shift (one fma) when modulated -- packed two-lane
+// fp32 ops, each lane rounded as the scalar op.
 __device__ __forceinline__ void norm_row_values(const NormArgs& a, long long row, int lane,
                                                 int chunk, const uint4& xr, float rstd,
                                                 float (&y)[8]) {
@@ -39,23 +42,25 @@ __device__ __forceinline__ void norm_row_values(const NormArgs& a, long long row
   const uint4 g = __ldg(reinterpret_cast<const uint4*>(a.gamma + col));
   const uint32_t xw[4] = {xr.x, xr.y, xr.z, xr.w};
   const uint32_t gw[4] = {g.x, g.y, g.z, g.w};
+  const float2 r2 = make_float2(rstd, rstd);
+  float2 v[4];
 #pragma unroll
-  for (int t = 0; t < 4; ++t) {
-    y[2 * t] = __uint_as_float(xw[t] << 16) * rstd * __uint_as_float(gw[t] << 16);
-    y[2 * t + 1] = __uint_as_float(xw[t] & 0xFFFF0000u) * rstd * __uint_as_float(gw[t] & 0xFFFF0000u);
-  }
+  for (int t = 0; t < 4; ++t) v[t] = mul2(mul2(bf16x2_to_f2(xw[t]), r2), bf16x2_to_f2(gw[t]));
   if (a.scale != nullptr) {
     const long long mrow = a.mod_idx ? a.mod_idx[row] : 0;
     const uint4 sc = __ldg(reinterpret_cast<const uint4*>(a.scale + mrow * a.K + col));
     const uint4 sh = __ldg(reinterpret_cast<const uint4*>(a.shift + mrow * a.K + col));
     const uint32_t cw[4] = {sc.x, sc.y, sc.z, sc.w};
     const uint32_t hw[4] = {sh.x, sh.y, sh.z, sh.w};
+    const float2 one = make_float2(1.0f, 1.0f);
 #pragma unroll
-    for (int t = 0; t < 4; ++t) {
-      y[2 * t] = fmaf(y[2 * t], 1.0f + __uint_as_float(cw[t] << 16), __uint_as_float(hw[t] << 16));
-      y[2 * t + 1] = fmaf(y[2 * t + 1], 1.0f + __uint_as_float(cw[t] & 0xFFFF0000u),
-                          __uint_as_float(hw[t] & 0xFFFF0000u));
-    }
+    for (int t = 0; t < 4; ++t)
+      v[t] = fma2(v[t], add2(one, bf16x2_to_f2(cw[t])), bf16x2_to_f2(hw[t]));
+  }
+#pragma unroll
+  for (int t = 0; t < 4; ++t) {
+    y[2 * t] = v[t].x;
+    y[2 * t + 1] = v[t].y;
   }
 }
 
@@ -148,21 +153,32 @@ __global__ void __launch_bounds__(kNormWarps * 32)
   const long long c4 = a.K >> 6;
   const bool live = row < a.M;
   const float rstd = live ? __ldg(rstd_in + row) : 0.f;
-  for (int c = 0; c < chunks; ++c) {
-    uint4 yr = make_uint4(0, 0, 0, 0);
-    if (live) {
-      const uint4 xr = ld_nc_v4(a.x + row * a.ldx + c * 256 + lane * 8);
-      float y[8];
-      norm_row_values(a, row, lane, c, xr, rstd, y);
-      yr = make_uint4(pack_bf16x2(y[0], y[1]), pack_bf16x2(y[2], y[3]), pack_bf16x2(y[4], y[5]),
-                      pack_bf16x2(y[6], y[7]));
-      if (y_out) *reinterpret_cast<uint4*>(y_out + row * a.K + c * 256 + lane * 8) = yr;
+  constexpr int U = 4;                         // 16-byte loads in flight per lane
+  for (int c0 = 0; c0 < chunks; c0 += U) {
+    uint4 xr[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      xr[u] = make_uint4(0, 0, 0, 0);
+      if (live && c0 + u < chunks) xr[u] = ld_nc_v4(a.x + row * a.ldx + (c0 + u) * 256 + lane * 8);
     }
-    uint32_t s8;
-    const uint32_t packed = quantize_half_block(yr, gs, d6, s8);
-    const long long hc = (long long)c * 32 + lane;        // 8-element half index in the row
-    *reinterpret_cast<uint32_t*>(q + row * (a.K >> 1) + hc * 4) = packed;
-    if ((lane & 1) == 0) sf[sf_swizzled_offset(row, hc >> 1, c4)] = static_cast<uint8_t>(s8);
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int c = c0 + u;
+      if (c >= chunks) break;                    // warp-uniform
+      uint4 yr = make_uint4(0, 0, 0, 0);
+      if (live) {
+        float y[8];
+        norm_row_values(a, row, lane, c, xr[u], rstd, y);
+        yr = make_uint4(pack_bf16x2(y[0], y[1]), pack_bf16x2(y[2], y[3]), pack_bf16x2(y[4], y[5]),
+                        pack_bf16x2(y[6], y[7]));
+        if (y_out) *reinterpret_cast<uint4*>(y_out + row * a.K + c * 256 + lane * 8) = yr;
+      }
+      uint32_t s8;
+      const uint32_t packed = quantize_half_block(yr, gs, d6, s8);
+      const long long hc = (long long)c * 32 + lane;        // 8-element half index in the row
+      *reinterpret_cast<uint32_t*>(q + row * (a.K >> 1) + hc * 4) = packed;
+      if ((lane & 1) == 0) sf[sf_swizzled_offset(row, hc >> 1, c4)] = static_cast<uint8_t>(s8);
+    }
   }
 }
 

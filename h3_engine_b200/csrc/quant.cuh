@@ -36,9 +36,18 @@ __device__ __forceinline__ float e4m3_to_f32(uint32_t b) {
   return (b & 0x80u) ? -v : v;
 }
 
+// e4m3fn bits (finite) -> fp32 through the hardware e4m3x2 -> f16x2 decode
+// (every finite e4m3 value is exact in f16; checked against e4m3_to_f32 on
+// all codes).
+__device__ __forceinline__ float e4m3_to_f32_hw(uint32_t b) {
+  uint32_t h2;
+  asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(h2) : "h"((uint16_t)b));
+  return __half2float(__ushort_as_half((unsigned short)(h2 & 0xFFFFu)));
+}
+
 // Two fp32 -> one byte of E2M1 codes: lo -> low nibble, hi -> high nibble,
-// round-to-nearest-even with saturation; the sign bit always follows the
-// input's sign (a negative value that rounds to zero becomes 0x8).
+// round-to-nearest-even with saturation.  The conversion keeps the sign of a
+// negative value that rounds to zero (0x8), as the recipe requires.
 __device__ __forceinline__ uint32_t f32x2_to_e2m1x2(float lo, float hi) {
   uint32_t r;
   asm("{\n\t.reg .b8 t;\n\t"
@@ -46,8 +55,15 @@ __device__ __forceinline__ uint32_t f32x2_to_e2m1x2(float lo, float hi) {
       "cvt.u32.u8 %0, t;\n\t}"
       : "=r"(r)
       : "f"(hi), "f"(lo));
-  const uint32_t sgn = ((__float_as_uint(lo) >> 31) << 3) | ((__float_as_uint(hi) >> 31) << 7);
-  return (r & 0xFFu) | sgn;
+  return r;
+}
+
+// Two IEEE round-to-nearest fp32 products in one instruction.
+__device__ __forceinline__ void mul_rn_f32x2(float a0, float a1, float b, float& d0, float& d1) {
+  asm("{\n\t.reg .b64 a, b, d;\n\tmov.b64 a, {%2, %3};\n\tmov.b64 b, {%4, %4};\n\t"
+      "mul.rn.f32x2 d, a, b;\n\tmov.b64 {%0, %1}, d;\n\t}"
+      : "=f"(d0), "=f"(d1)
+      : "f"(a0), "f"(a1), "f"(b));
 }
 
 // Byte offset of scale (r, c) in the 128x4-tile layout (c4 = C/4 tiles per row block).
@@ -57,29 +73,26 @@ __device__ __forceinline__ int64_t sf_swizzled_offset(int64_t r, int64_t c, int6
 
 // Quantize 8 consecutive bf16 values (one lane's half of a 16-block; the
 // partner half sits in the neighbouring lane).  Returns 4 packed code bytes
-// and the block's scale byte.
+// and the block's scale byte.  The block max is taken on the bf16 bit
+// patterns: |x| of a bf16 is its bits & 0x7FFF, and non-negative bf16 values
+// order like their 16-bit integers (NaN inputs are outside the recipe).
 __device__ __forceinline__ uint32_t quantize_half_block(const uint4& raw, float gs, float d6,
                                                         uint32_t& s8_out) {
   const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
-  float v[8];
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    v[2 * i] = __uint_as_float(w[i] << 16);
-    v[2 * i + 1] = __uint_as_float(w[i] & 0xFFFF0000u);
-  }
-  float m = 0.f;
-#pragma unroll
-  for (int i = 0; i < 8; ++i) m = fmaxf(m, fabsf(v[i]));
-  m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 1));
+  uint32_t m2 = __vmaxu2(w[0] & 0x7FFF7FFFu, w[1] & 0x7FFF7FFFu);
+  m2 = __vmaxu2(m2, __vmaxu2(w[2] & 0x7FFF7FFFu, w[3] & 0x7FFF7FFFu));
+  uint32_t mb = max(m2 & 0xFFFFu, m2 >> 16);
+  mb = max(mb, __shfl_xor_sync(0xffffffffu, mb, 1));
+  const float m = __uint_as_float(mb << 16);
   const uint32_t s8 = f32_to_e4m3_sat(__fdiv_rn(m, d6));
-  const float d = __fmul_rn(e4m3_to_f32(s8), gs);
+  const float d = __fmul_rn(e4m3_to_f32_hw(s8), gs);
   uint32_t packed = 0;
   if (d != 0.f) {
     const float inv = __frcp_rn(d);
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
-      const float a = __fmul_rn(v[2 * i], inv);
-      const float b = __fmul_rn(v[2 * i + 1], inv);
+      float a, b;
+      mul_rn_f32x2(__uint_as_float(w[i] << 16), __uint_as_float(w[i] & 0xFFFF0000u), inv, a, b);
       packed |= f32x2_to_e2m1x2(a, b) << (8 * i);
     }
   }
@@ -88,11 +101,12 @@ __device__ __forceinline__ uint32_t quantize_half_block(const uint4& raw, float 
 }
 
 constexpr int kQuantThreads = 256;
-constexpr int kQuantUnroll = 2;
+constexpr int kQuantUnroll = 4;
 
-// Two lanes per 16-element block; each lane loads 16 bytes.  A warp covers
-// 16 consecutive blocks (1 KiB of bf16) of one row: reads and code writes
-// are fully coalesced.
+// One warp per row (grid-stride over rows), two lanes per 16-element block,
+// each lane one 16-byte load; kQuantUnroll loads in flight per lane.  Reads
+// and code writes of a warp are contiguous 512-byte / 128-byte runs.  Rows
+// in [M, Mpad) are padding: they quantize zeros (codes and scales 0).
 template <int LAYOUT>
 __global__ void __launch_bounds__(kQuantThreads)
     k_nvfp4_quantize(const __nv_bfloat16* __restrict__ x, int64_t M, int64_t K, int64_t ldx,
@@ -103,37 +117,37 @@ __global__ void __launch_bounds__(kQuantThreads)
   if (gs_out != nullptr && blockIdx.x == 0 && threadIdx.x == 0) *gs_out = gs;
 
   const int lane = threadIdx.x & 31;
-  const int64_t hpr = K >> 3;                 // 8-element halves per row
-  const int64_t total = Mpad * hpr;           // even
+  const int hpr = (int)(K >> 3);              // 8-element halves per row (even)
   const int64_t kq = K >> 1;                  // code bytes per row
   const int64_t c_row = K >> 4;               // scales per row
   const int64_t c4 = K >> 6;
-  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
-  for (int64_t base = (int64_t)blockIdx.x * blockDim.x + (threadIdx.x & ~31); base < total;
-       base += stride * kQuantUnroll) {
-    uint4 raw[kQuantUnroll];
-    int64_t row[kQuantUnroll], hc[kQuantUnroll];
-    bool valid[kQuantUnroll];
+  const int64_t warps = (int64_t)gridDim.x * (kQuantThreads / 32);
+  for (int64_t r = (int64_t)blockIdx.x * (kQuantThreads / 32) + (threadIdx.x >> 5); r < Mpad;
+       r += warps) {
+    const bool real = r < M;
+    const __nv_bfloat16* xr = x + r * ldx;
+    uint8_t* qr = q + r * kq;
+    for (int h0 = 0; h0 < hpr; h0 += 32 * kQuantUnroll) {
+      uint4 raw[kQuantUnroll];
 #pragma unroll
-    for (int u = 0; u < kQuantUnroll; ++u) {
-      const int64_t h = base + u * stride + lane;
-      valid[u] = h < total;
-      row[u] = valid[u] ? h / hpr : 0;
-      hc[u] = h - row[u] * hpr;
-      raw[u] = make_uint4(0, 0, 0, 0);
-      if (valid[u] && row[u] < M) raw[u] = ld_nc_v4(x + row[u] * ldx + hc[u] * 8);
-    }
+      for (int u = 0; u < kQuantUnroll; ++u) {
+        const int h = h0 + u * 32 + lane;
+        raw[u] = make_uint4(0, 0, 0, 0);
+        if (real && h < hpr) raw[u] = ld_nc_v4(xr + (int64_t)h * 8);
+      }
 #pragma unroll
-    for (int u = 0; u < kQuantUnroll; ++u) {
-      uint32_t s8;
-      const uint32_t packed = quantize_half_block(raw[u], gs, d6, s8);
-      if (valid[u]) {
-        *reinterpret_cast<uint32_t*>(q + row[u] * kq + hc[u] * 4) = packed;
-        if ((lane & 1) == 0) {
-          const int64_t c = hc[u] >> 1;
-          const int64_t off = LAYOUT == H3B_SF_SWIZZLED ? sf_swizzled_offset(row[u], c, c4)
-                                                        : row[u] * c_row + c;
-          sf[off] = static_cast<uint8_t>(s8);
+      for (int u = 0; u < kQuantUnroll; ++u) {
+        const int h = h0 + u * 32 + lane;
+        uint32_t s8;
+        const uint32_t packed = quantize_half_block(raw[u], gs, d6, s8);
+        if (h < hpr) {
+          *reinterpret_cast<uint32_t*>(qr + (int64_t)h * 4) = packed;
+          if ((lane & 1) == 0) {
+            const int64_t c = h >> 1;
+            const int64_t off = LAYOUT == H3B_SF_SWIZZLED ? sf_swizzled_offset(r, c, c4)
+                                                          : r * c_row + c;
+            sf[off] = static_cast<uint8_t>(s8);
+          }
         }
       }
     }

@@ -35,69 +35,101 @@ struct RopeArgs {
 };
 
 constexpr int kRopeWarps = 8;
+constexpr int kRopeUnroll = 4;       // 16-byte loads in flight per lane
 
-// One warp per head vector; lane l holds elements [l*D/32, (l+1)*D/32).
-// The rotate-half partner of element j (j +- R/2) lives in another lane and
-// is fetched with a shuffle (R/2 is a multiple of D/32, so slots line up).
+// One warp per token row (grid-stride over rows).  A head vector of D values
+// is spread over LPH = D/8 lanes, 8 consecutive values (one 16-byte load) per
+// lane, so one warp instruction covers 32/LPH head vectors of the row's 2H
+// (q heads then k heads).  The row's cos / sin values of a lane's 8 columns
+// (bf16-rounded) and its norm weights are loaded once per row / once per
+// warp.  The sum of squares reduces over the LPH lanes of a head; the
+// rotate-half partner of column j (j +- R/2, R/2 a multiple of 8) is the
+// lane (R/2)/8 away in the same head, fetched with shuffles.
 template <int D>
 __global__ void __launch_bounds__(kRopeWarps * 32) k_qk_norm_rope(const RopeArgs a) {
-  constexpr int EPL = D / 32;     // elements per lane (2 or 4)
+  constexpr int LPH = D / 8;                 // lanes per head vector
+  constexpr int HPW = 32 / LPH;              // head vectors per warp instruction
   const int lane = threadIdx.x & 31;
-  const long long total = a.T * 2 * a.H;
+  const int sub = lane % LPH;
+  const int j0 = sub * 8;                    // first column of this lane
+  const int half = a.R >> 1;
+  const bool rot = a.cos != nullptr && j0 < a.R;
+  const int partner = (lane - sub) + (j0 < half ? (j0 + half) >> 3 : (j0 - half) >> 3);
+  float gq[8], gk[8];
+#pragma unroll
+  for (int e = 0; e < 8; ++e) {
+    gq[e] = a.wq ? __bfloat162float(a.wq[j0 + e]) : 1.f;
+    gk[e] = a.wk ? __bfloat162float(a.wk[j0 + e]) : 1.f;
+  }
+  const int nv = 2 * a.H;                    // head vectors per row
   const long long warp_id = (long long)blockIdx.x * kRopeWarps + (threadIdx.x >> 5);
   const long long nwarps = (long long)gridDim.x * kRopeWarps;
-  const int half = a.R >> 1;
-  for (long long w = warp_id; w < total; w += nwarps) {
-    const long long t = w / (2 * a.H);
-    const int v = (int)(w - t * 2 * a.H);
-    const bool is_k = v >= a.H;
-    const int h = is_k ? v - a.H : v;
-    __nv_bfloat16* p = (is_k ? a.k + t * a.k_stride + a.k_off : a.q + t * a.q_stride + a.q_off) +
-                       (long long)h * D + lane * EPL;
-    float x[EPL];
-    if (EPL == 4) {
-      const uint2 r = *reinterpret_cast<const uint2*>(p);
-      x[0] = __uint_as_float(r.x << 16);
-      x[1] = __uint_as_float(r.x & 0xFFFF0000u);
-      x[2] = __uint_as_float(r.y << 16);
-      x[3] = __uint_as_float(r.y & 0xFFFF0000u);
-    } else {
-      const uint32_t r = *reinterpret_cast<const uint32_t*>(p);
-      x[0] = __uint_as_float(r << 16);
-      x[1] = __uint_as_float(r & 0xFFFF0000u);
-    }
-    const __nv_bfloat16* wp = is_k ? a.wk : a.wq;
-    if (wp != nullptr) {
-      float ss = 0.f;
+  for (long long t = warp_id; t < a.T; t += nwarps) {
+    float c[8], s[8];
+    if (rot) {
+      const float4* cp = reinterpret_cast<const float4*>(a.cos + t * a.cs_stride + j0);
+      const float4* sp = reinterpret_cast<const float4*>(a.sin + t * a.cs_stride + j0);
+      const float4 c0 = __ldg(cp), c1 = __ldg(cp + 1), s0 = __ldg(sp), s1 = __ldg(sp + 1);
+      const float cv[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+      const float sv[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
 #pragma unroll
-      for (int e = 0; e < EPL; ++e) ss = fmaf(x[e], x[e], ss);
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-      const float rstd = rsqrtf(ss / (float)D + a.eps);
-#pragma unroll
-      for (int e = 0; e < EPL; ++e) x[e] = x[e] * rstd * __bfloat162float(wp[lane * EPL + e]);
-    }
-    if (a.cos != nullptr) {
-      const int j0 = lane * EPL;
-      const int plane = j0 < half ? (j0 + half) / EPL : (j0 - half) / EPL;
-      float xp[EPL];
-#pragma unroll
-      for (int e = 0; e < EPL; ++e) xp[e] = __shfl_sync(0xffffffffu, x[e], plane & 31);
-      if (j0 < a.R) {
-        const float* cp = a.cos + t * a.cs_stride + j0;
-        const float* sp = a.sin + t * a.cs_stride + j0;
-#pragma unroll
-        for (int e = 0; e < EPL; ++e) {
-          const float c = __bfloat162float(__float2bfloat16_rn(__ldg(cp + e)));
-          const float s = __bfloat162float(__float2bfloat16_rn(__ldg(sp + e)));
-          x[e] = j0 < half ? fmaf(x[e], c, -xp[e] * s) : fmaf(x[e], c, xp[e] * s);
-        }
+      for (int e = 0; e < 8; ++e) {
+        c[e] = __bfloat162float(__float2bfloat16_rn(cv[e]));
+        s[e] = __bfloat162float(__float2bfloat16_rn(sv[e]));
       }
     }
-    if (EPL == 4) {
-      *reinterpret_cast<uint2*>(p) = make_uint2(pack_bf16x2(x[0], x[1]), pack_bf16x2(x[2], x[3]));
-    } else {
-      *reinterpret_cast<uint32_t*>(p) = pack_bf16x2(x[0], x[1]);
+    __nv_bfloat16* qrow = a.q + t * a.q_stride + a.q_off;
+    __nv_bfloat16* krow = a.k + t * a.k_stride + a.k_off;
+    for (int v0 = 0; v0 < nv; v0 += HPW * kRopeUnroll) {
+      uint4 raw[kRopeUnroll];
+      __nv_bfloat16* ptr[kRopeUnroll];
+      bool is_k[kRopeUnroll], valid[kRopeUnroll];
+#pragma unroll
+      for (int u = 0; u < kRopeUnroll; ++u) {
+        const int v = v0 + u * HPW + lane / LPH;
+        valid[u] = v < nv;
+        is_k[u] = v >= a.H;
+        const int h = is_k[u] ? v - a.H : v;
+        ptr[u] = (is_k[u] ? krow : qrow) + (long long)h * D + j0;
+        raw[u] = valid[u] ? *reinterpret_cast<const uint4*>(ptr[u]) : make_uint4(0, 0, 0, 0);
+      }
+#pragma unroll
+      for (int u = 0; u < kRopeUnroll; ++u) {
+        const uint32_t w[4] = {raw[u].x, raw[u].y, raw[u].z, raw[u].w};
+        float x[8];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          x[2 * i] = __uint_as_float(w[i] << 16);
+          x[2 * i + 1] = __uint_as_float(w[i] & 0xFFFF0000u);
+        }
+        // the reduction runs on every lane (the head vectors of one warp
+        // instruction may mix q and k heads, with and without a norm weight)
+        float ss = 0.f;
+#pragma unroll
+        for (int e = 0; e < 8; ++e) ss = fmaf(x[e], x[e], ss);
+#pragma unroll
+        for (int o = LPH / 2; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+        if (is_k[u] ? a.wk != nullptr : a.wq != nullptr) {
+          const float rstd = rsqrtf(ss / (float)D + a.eps);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) x[e] = x[e] * rstd * (is_k[u] ? gk[e] : gq[e]);
+        }
+        if (a.cos != nullptr) {
+          float xp[8];
+#pragma unroll
+          for (int e = 0; e < 8; ++e) xp[e] = __shfl_sync(0xffffffffu, x[e], partner);
+          if (rot) {
+#pragma unroll
+            for (int e = 0; e < 8; ++e)
+              x[e] = j0 < half ? fmaf(x[e], c[e], -xp[e] * s[e]) : fmaf(x[e], c[e], xp[e] * s[e]);
+          }
+        }
+        if (valid[u]) {
+          *reinterpret_cast<uint4*>(ptr[u]) =
+              make_uint4(pack_bf16x2(x[0], x[1]), pack_bf16x2(x[2], x[3]),
+                         pack_bf16x2(x[4], x[5]), pack_bf16x2(x[6], x[7]));
+        }
+      }
     }
   }
 }

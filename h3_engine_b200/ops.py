@@ -244,8 +244,9 @@ def qk_norm_rope(qkv: torch.Tensor, heads: int, head_dim: int, *, q_off: int, k_
             raise TypeError("cos/sin must be fp32")
         cos = cos.reshape(T, -1)
         sin = sin.reshape(T, -1)
-        if cos.stride(-1) != 1 or sin.stride(-1) != 1 or cos.stride(0) != sin.stride(0):
-            cos, sin = cos.contiguous(), sin.contiguous()
+        if (cos.stride(-1) != 1 or sin.stride(-1) != 1 or cos.stride(0) != sin.stride(0)
+                or cos.stride(0) % 4 or cos.data_ptr() % 16 or sin.data_ptr() % 16):
+            cos, sin = cos.contiguous().clone(), sin.contiguous().clone()
         R, cs = cos.shape[1], cos.stride(0)
     st = _lib.lib().h3b_qk_norm_rope(_p(q2), q2.stride(0), q_off, _p(k2), k2.stride(0), k_off, T,
                                      heads, head_dim, _p(wq), _p(wk), float(eps), _p(cos),
