@@ -104,24 +104,25 @@ __global__ void __launch_bounds__(kNormWarps * 32)
     for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
     const float rstd = rsqrtf(ss / (float)a.K + a.eps);
     if (lane == 0) rstd_out[row] = rstd;
+    // |bf16(y)| max on packed bit patterns (non-negative bf16 values order
+    // like their 16-bit integers)
+    uint32_t mb2 = 0;
+    auto amax_y = [&](int c, const uint4& v) {
+      float y[8];
+      norm_row_values(a, row, lane, c, v, rstd, y);
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+        mb2 = __vmaxu2(mb2, pack_bf16x2(y[2 * i], y[2 * i + 1]) & 0x7FFF7FFFu);
+    };
     if (CACHE > 0) {
 #pragma unroll
-      for (int c = 0; c < NR; ++c) {
-        if (c < chunks) {
-          float y[8];
-          norm_row_values(a, row, lane, c, xr[c], rstd, y);
-#pragma unroll
-          for (int i = 0; i < 8; ++i) m = fmaxf(m, fabsf(__bfloat162float(__float2bfloat16_rn(y[i]))));
-        }
-      }
+      for (int c = 0; c < NR; ++c)
+        if (c < chunks) amax_y(c, xr[c]);
     } else {
-      for (int c = 0; c < chunks; ++c) {
-        float y[8];
-        norm_row_values(a, row, lane, c, __ldg(reinterpret_cast<const uint4*>(xp + c * 256)), rstd, y);
-#pragma unroll
-        for (int i = 0; i < 8; ++i) m = fmaxf(m, fabsf(__bfloat162float(__float2bfloat16_rn(y[i]))));
-      }
+      for (int c = 0; c < chunks; ++c)
+        amax_y(c, __ldg(reinterpret_cast<const uint4*>(xp + c * 256)));
     }
+    m = __uint_as_float(max(mb2 & 0xFFFFu, mb2 >> 16) << 16);
   }
   // CTA-wide max then one atomic
 #pragma unroll
