@@ -74,7 +74,7 @@ def _worker(rank, world, port, total, q):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("world,total", [(2, 37), (4, 37), (4, 40)])
+@pytest.mark.parametrize("world,total", [(2, 37), (4, 37), (4, 40), (8, 37), (8, 33784)])
 def test_collectives_on_gloo_ranks(world, total):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
