@@ -203,6 +203,46 @@ class AttnBlock(_GemmTimer):
         per_row = self.hidden // 16           # scale bytes per weight row (blocked layout)
         return self.sf_qkv[r0 * per_row:r1 * per_row]
 
+    def _sharded_attention(self, qh, sfh, gsh, T, ws, dev, cos, sin, cu_seqlens, shard):
+        """Token-sharded attention: this rank's K|V rows (projection + key
+        norm/RoPE) go into its chunk of the full-sequence buffer and are
+        all-gathered on a side stream while the query projection and its
+        norm/RoPE run; one attention launch then covers every head.  Every
+        byte equals the unsharded run's (GEMM columns do not depend on the N
+        split; attention heads are independent)."""
+        HD, H, D = self.inner, self.heads, self.head_dim
+        q = _buf(ws, "q", (T, HD), torch.bfloat16, dev)
+        kv = _buf(ws, "kv", (shard.buffer_rows(), 2 * HD), torch.bfloat16, dev)
+        kv_local = kv[shard.row0:shard.row0 + T]
+        main = torch.cuda.current_stream(dev)
+        side = ws.get("side")
+        if side is None:
+            side = ws["side"] = torch.cuda.Stream(device=dev)
+        ev = self._event()
+        ops.gemm(qh, sfh, gsh, T, self.w_qkv[HD:], self._sf_rows(HD, 3 * HD), self.gs_qkv[1:],
+                 2 * HD, self.hidden, gsb_seg=HD, out=kv_local)
+        ops.qk_norm_rope(kv_local, H, D, q_off=0, k_off=0, wq=None, wk=self.norm_k,
+                         eps=self.qk_eps, cos=cos, sin=sin, heads_q=False)
+        ready = torch.cuda.Event()
+        ready.record(main)
+        side.wait_event(ready)
+        with torch.cuda.stream(side):
+            shard.all_gather(kv, kv_local)
+            gathered = torch.cuda.Event()
+            gathered.record(side)
+        ops.gemm(qh, sfh, gsh, T, self.w_qkv[:HD], self._sf_rows(0, HD), self.gs_qkv[:1], HD,
+                 self.hidden, out=q)
+        ops.qk_norm_rope(q, H, D, q_off=0, k_off=0, wq=self.norm_q, wk=None, eps=self.qk_eps,
+                         cos=cos, sin=sin, heads_k=False)
+        self._event(ev)
+        main.wait_event(gathered)        # also orders the next block's writes after the gather
+        ev = self._event(sink=self.attn_events)
+        o = ops.attention_varlen(q, H, D, cu_seqlens, q_off=0, k_off=0, v_off=HD,
+                                 kv=kv[:shard.total], q_row0=shard.row0,
+                                 out=_buf(ws, "o", (T, HD), torch.bfloat16, dev))
+        self._event(ev, sink=self.attn_events)
+        return o
+
     def __call__(self, x: torch.Tensor, rope: tuple[torch.Tensor, torch.Tensor] | None,
                  cu_seqlens, out: torch.Tensor | None = None, *,
                  shift: torch.Tensor | None = None, scale: torch.Tensor | None = None,
@@ -234,24 +274,7 @@ class AttnBlock(_GemmTimer):
         else:
             if shard.rows != T:
                 raise ValueError("shard rows do not match the local activation")
-            q = _buf(ws, "q", (T, HD), torch.bfloat16, dev)
-            kv = _buf(ws, "kv", (shard.buffer_rows(), 2 * HD), torch.bfloat16, dev)
-            kv_local = kv[shard.row0:shard.row0 + T]
-            ev = self._event()
-            ops.gemm(qh, sfh, gsh, T, self.w_qkv[:HD], self._sf_rows(0, HD), self.gs_qkv[:1], HD,
-                     self.hidden, out=q)
-            ops.gemm(qh, sfh, gsh, T, self.w_qkv[HD:], self._sf_rows(HD, 3 * HD),
-                     self.gs_qkv[1:], 2 * HD, self.hidden, gsb_seg=HD, out=kv_local)
-            self._event(ev)
-            ops.qk_norm_rope(q, H, D, q_off=0, k_off=0, wq=self.norm_q, wk=self.norm_k,
-                             eps=self.qk_eps, cos=cos, sin=sin, k_buf=kv_local)
-            shard.all_gather(kv, kv_local)
-            ev = self._event(sink=self.attn_events)
-            o = ops.attention_varlen(q, H, D, cu_seqlens, q_off=0, k_off=0, v_off=HD,
-                                     kv=kv[:shard.total],
-                                     q_row0=shard.row0,
-                                     out=_buf(ws, "o", (T, HD), torch.bfloat16, dev))
-            self._event(ev, sink=self.attn_events)
+            o = self._sharded_attention(qh, sfh, gsh, T, ws, dev, cos, sin, cu_seqlens, shard)
         mp = qh.shape[0]
         amax_o = ops.amax(o, out=_buf(ws, "amax_o", (1,), torch.float32, dev))
         if hook is not None:

@@ -366,8 +366,8 @@ int h3b_qk_norm_rope(void* q, int64_t q_stride, int64_t q_off, void* k, int64_t 
     return H3B_ERR_INVALID_ARG;
   if ((q_stride | k_stride | q_off | k_off) % 8) return H3B_ERR_ALIGNMENT;
   if (T == 0) return H3B_OK;
-  if (!q || !k) return H3B_ERR_INVALID_ARG;
-  if (!aligned16(q) || !aligned16(k)) return H3B_ERR_ALIGNMENT;
+  if (!q && !k) return H3B_ERR_INVALID_ARG;            // NULL q or k: those heads are skipped
+  if ((q && !aligned16(q)) || (k && !aligned16(k))) return H3B_ERR_ALIGNMENT;
   RopeArgs a;
   a.q = static_cast<__nv_bfloat16*>(q);
   a.k = static_cast<__nv_bfloat16*>(k);
@@ -377,6 +377,8 @@ int h3b_qk_norm_rope(void* q, int64_t q_stride, int64_t q_off, void* k, int64_t 
   a.q_off = q_off;
   a.k_off = k_off;
   a.H = H;
+  a.hq = q ? H : 0;
+  a.hk = k ? H : 0;
   a.R = R;
   a.wq = static_cast<const __nv_bfloat16*>(wq);
   a.wk = static_cast<const __nv_bfloat16*>(wk);

@@ -25,6 +25,7 @@ struct RopeArgs {
   long long T, q_stride, k_stride;
   long long q_off, k_off;
   int H;                   // heads per block
+  int hq, hk;              // query / key heads processed (H or 0)
   int R;                   // rotary dims (even, <= D)
   const __nv_bfloat16* wq; // [D] or null
   const __nv_bfloat16* wk; // [D] or null
@@ -61,7 +62,7 @@ __global__ void __launch_bounds__(kRopeWarps * 32) k_qk_norm_rope(const RopeArgs
     gq[e] = a.wq ? __bfloat162float(a.wq[j0 + e]) : 1.f;
     gk[e] = a.wk ? __bfloat162float(a.wk[j0 + e]) : 1.f;
   }
-  const int nv = 2 * a.H;                    // head vectors per row
+  const int nv = a.hq + a.hk;                // head vectors per row (q heads, then k heads)
   const long long warp_id = (long long)blockIdx.x * kRopeWarps + (threadIdx.x >> 5);
   const long long nwarps = (long long)gridDim.x * kRopeWarps;
   for (long long t = warp_id; t < a.T; t += nwarps) {
@@ -78,8 +79,8 @@ __global__ void __launch_bounds__(kRopeWarps * 32) k_qk_norm_rope(const RopeArgs
         s[e] = __bfloat162float(__float2bfloat16_rn(sv[e]));
       }
     }
-    __nv_bfloat16* qrow = a.q + t * a.q_stride + a.q_off;
-    __nv_bfloat16* krow = a.k + t * a.k_stride + a.k_off;
+    __nv_bfloat16* qrow = a.hq ? a.q + t * a.q_stride + a.q_off : nullptr;
+    __nv_bfloat16* krow = a.hk ? a.k + t * a.k_stride + a.k_off : nullptr;
     for (int v0 = 0; v0 < nv; v0 += HPW * kRopeUnroll) {
       uint4 raw[kRopeUnroll];
       __nv_bfloat16* ptr[kRopeUnroll];
@@ -88,8 +89,8 @@ __global__ void __launch_bounds__(kRopeWarps * 32) k_qk_norm_rope(const RopeArgs
       for (int u = 0; u < kRopeUnroll; ++u) {
         const int v = v0 + u * HPW + lane / LPH;
         valid[u] = v < nv;
-        is_k[u] = v >= a.H;
-        const int h = is_k[u] ? v - a.H : v;
+        is_k[u] = v >= a.hq;
+        const int h = is_k[u] ? v - a.hq : v;
         ptr[u] = (is_k[u] ? krow : qrow) + (long long)h * D + j0;
         raw[u] = valid[u] ? *reinterpret_cast<const uint4*>(ptr[u]) : make_uint4(0, 0, 0, 0);
       }

@@ -225,10 +225,14 @@ def rmsnorm_quantize(x: torch.Tensor, gamma: torch.Tensor, eps: float, *,
 def qk_norm_rope(qkv: torch.Tensor, heads: int, head_dim: int, *, q_off: int, k_off: int,
                  wq: torch.Tensor | None, wk: torch.Tensor | None, eps: float,
                  cos: torch.Tensor | None = None, sin: torch.Tensor | None = None,
-                 k_buf: torch.Tensor | None = None) -> torch.Tensor:
+                 k_buf: torch.Tensor | None = None, heads_q: bool = True,
+                 heads_k: bool = True) -> torch.Tensor:
     """In-place per-head RMSNorm + rotate-half RoPE on the query heads of
     ``qkv`` (at ``q_off``) and the key heads of ``k_buf`` (default ``qkv``, at
-    ``k_off``), both bf16 ``[T, stride]``.  ``cos``/``sin``: fp32 ``[T, R]``."""
+    ``k_off``), both bf16 ``[T, stride]``.  ``cos``/``sin``: fp32 ``[T, R]``.
+    ``heads_q`` / ``heads_k`` False skips the query / key heads."""
+    if not (heads_q or heads_k):
+        raise ValueError("nothing to do: both query and key heads skipped")
     dev = _need_cuda(qkv, wq, wk, cos, sin, k_buf)
     q2 = qkv.reshape(-1, qkv.shape[-1]) if qkv.dim() != 2 else qkv
     k2 = q2 if k_buf is None else (k_buf.reshape(-1, k_buf.shape[-1]) if k_buf.dim() != 2 else k_buf)
@@ -248,7 +252,8 @@ def qk_norm_rope(qkv: torch.Tensor, heads: int, head_dim: int, *, q_off: int, k_
                 or cos.stride(0) % 4 or cos.data_ptr() % 16 or sin.data_ptr() % 16):
             cos, sin = cos.contiguous().clone(), sin.contiguous().clone()
         R, cs = cos.shape[1], cos.stride(0)
-    st = _lib.lib().h3b_qk_norm_rope(_p(q2), q2.stride(0), q_off, _p(k2), k2.stride(0), k_off, T,
+    st = _lib.lib().h3b_qk_norm_rope(_p(q2) if heads_q else None, q2.stride(0), q_off,
+                                     _p(k2) if heads_k else None, k2.stride(0), k_off, T,
                                      heads, head_dim, _p(wq), _p(wk), float(eps), _p(cos),
                                      _p(sin), R, cs, _stream(dev))
     _lib.check(st, "h3b_qk_norm_rope")

@@ -151,7 +151,8 @@ H3B_API int h3b_rmsnorm_quantize(const void* x, int64_t M, int64_t K, int64_t ld
  * Replaces qk_norm + apply_rotary_emb / norm_rope
  * (h3_inference/kernels/elementwise_norm_rope.py:19-40,104-148).
  * D in {64, 128}; R <= D, (R/2) % 8 == 0; q/k strides and offsets
- * multiples of 8; cos/sin 16-byte aligned with cs_stride % 4 == 0.        */
+ * multiples of 8; cos/sin 16-byte aligned with cs_stride % 4 == 0.  q or k
+ * may be NULL (only the other heads are processed), not both.             */
 H3B_API int h3b_qk_norm_rope(void* q, int64_t q_stride, int64_t q_off, void* k, int64_t k_stride,
                              int64_t k_off, int64_t T, int H, int D, const void* wq,
                              const void* wk, float eps, const float* cos, const float* sin, int R,

@@ -112,10 +112,15 @@ def test_sharded_attn_block_reproduces_unsharded(cuda):
             t.copy_(ref)
             seen.append(1)
 
+        calls = []
+
         def all_gather(kv, local):
+            calls.append(1)
             assert torch.equal(local, kv_ref[a:b])        # local K|V after norm + RoPE
-            kv.copy_(kv_ref)
+            kv[:T].copy_(kv_ref)
 
         shard = SequenceShard(a, b - a, T, all_gather, reduce_max)
         y = blk(x[a:b], (cos[a:b], sin[a:b]), cu, shard=shard)
+        torch.cuda.synchronize()
+        assert calls == [1]
         assert torch.equal(y, full[a:b])
