@@ -38,9 +38,22 @@ def _run(cuda, q, k, v, cu):
     return o.float().cpu().numpy().reshape(T, H, D), qkv
 
 
+def _cu(lens):
+    cu = [0]
+    for n in lens:
+        cu.append(cu[-1] + n)
+    return cu
+
+
+# 64 documents (the kernel's maximum): empty, single-token, tile-edge
+# (127/128/129, 255/256/257) and ragged lengths
+RAGGED = _cu([0, 1, 2, 127, 128, 129, 255, 256, 257, 3, 64, 0, 5, 1]
+             + [17 * (i % 9) + 1 for i in range(50)])
+
+
 @pytest.mark.gpu
 @pytest.mark.parametrize("cu,H", [([0, 128], 1), ([0, 300, 700], 2), ([0, 1000, 1050, 1300], 3),
-                                  ([0, 2048], 4)])
+                                  ([0, 2048], 4), (RAGGED, 2)])
 def test_kernel_matches_oracle(cuda, cu, H):
     T, D = cu[-1], 128
     q, k, v = _qkv(T, H, D, seed=len(cu) + H)

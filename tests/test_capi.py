@@ -60,3 +60,22 @@ def test_host_validation_rejects_bad_shapes_without_gpu():
     # M == 0 is a no-op that succeeds without touching memory
     assert g(p, p, None, 0, 128, p, p, None, 0, 256, 256, None, None, 0, None, None, 0, p, 256, None, None) == 0
     assert lib.h3b_nvfp4_dequantize(p, p, 1, 100, None, 4, 64, p, None) == 1
+
+
+def test_attention_rejects_bad_documents():
+    """Argument checks of h3b_attention_varlen that run before any CUDA call."""
+    import ctypes
+    from h3_engine_b200 import _lib
+    lib = _lib.lib()
+    p = ctypes.c_void_p(16 * 1024)
+
+    def call(cu, kv_rows, ndocs=None):
+        arr = (ctypes.c_int32 * len(cu))(*cu)
+        n = len(cu) - 1 if ndocs is None else ndocs
+        return lib.h3b_attention_varlen(p, kv_rows, 768, 0, 0, p, kv_rows, 768, 256, 512, 2, 128,
+                                        arr, n, 0.088, p, 256, None)
+
+    assert call(list(range(66)), 65) == 1                 # 65 documents > 64
+    assert call([0, 10, 20], 21) == 1                     # cu[-1] != rows
+    assert call([0, 12, 10, 20], 20) == 1                 # decreasing offsets
+    assert call([1, 10, 20], 20) == 1                     # cu[0] != 0
