@@ -33,6 +33,9 @@ from . import ops
 from .nvfp4 import NVFP4Weight
 
 
+_GEMM_SINK = object()
+
+
 class _GemmTimer:
     """When ``gemm_events`` / ``attn_events`` are lists, (start, end) CUDA
     events are appended around every GEMM / attention launch on the current
@@ -41,8 +44,11 @@ class _GemmTimer:
     gemm_events: list | None = None
     attn_events: list | None = None
 
-    def _event(self, start=None, sink=None):
-        sink = self.gemm_events if sink is None else sink
+    def _event(self, start=None, sink=_GEMM_SINK):
+        """Record an event; with ``start`` append (start, event) to ``sink``
+        (default the GEMM list; a None sink records nothing)."""
+        if sink is _GEMM_SINK:
+            sink = self.gemm_events
         if sink is None:
             return None
         e = torch.cuda.Event(enable_timing=True)

@@ -18,14 +18,15 @@ namespace h3b {
 // CTAs reuse it from L2).  The producer and the MMA issuer run ahead across
 // tile boundaries, so the operand pipeline never drains between tiles.
 //   warp 0     TMA producer (3-stage ring, 54 KiB per stage)
-//   warp 1     TMEM allocator + single-thread MMA issuer
+//   warp 1     TMEM allocator + MMA issuer: the whole warp runs the issue loop
+//              and one elected lane issues each tcgen05.cp / mma / commit
 //   warps 2-9  epilogue, two warps per TMEM lane quadrant (128 columns each):
 //              they pull the whole 128x256 fp32 accumulator into registers,
 //              hand TMEM back to the MMA warp (acc_empty, 8 arrivals), then
-//              apply alpha / bias / GELU / residual, convert to bf16, stage
-//              64-column chunks in a 128B-swizzled 4 KiB buffer per warp and
-//              write them with TMA stores (which clip rows >= M), while the
-//              next tile's mainloop runs.
+//              apply alpha / bias / GELU (or SwiGLU) / gate / residual,
+//              convert to bf16, stage 64-column chunks in a 128B-swizzled
+//              4 KiB buffer per warp and write them with TMA stores (which
+//              clip rows >= M), while the next tile's mainloop runs.
 // Every wait is bounded; there is no barrier among the epilogue warps, so a
 // timeout in one role always unwinds the whole CTA.
 // ============================================================================
