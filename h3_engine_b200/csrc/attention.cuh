@@ -18,7 +18,10 @@
 //               the other tile's softmax runs:
 //                 QK_A(0) QK_B(0) | PV_A(j) QK_A(j+1) PV_B(j) QK_B(j+1) | ...
 //               S = Q K^T: tcgen05.mma kind::f16, SS, M=128 N=128 K=16 x8;
-//               O += P V: TS form, P read from tensor memory, V MN-major.
+//               O += P V: TS form, P read from tensor memory, V MN-major,
+//               issued in two halves: keys [0, 64) as soon as softmax has
+//               stored their P (p_half), the rest on p_full, so the first
+//               half runs under the second half's exponentials.
 //               P_X(j) lives in the columns of S_X; QK_X(j+1) overwrites them
 //               only after PV_X(j), in issue order.
 //   warps 0-3   softmax of tile A, warps 4-7 of tile B (one query row per
@@ -125,12 +128,13 @@ constexpr uint32_t kPolyPairs = 0x52u;   // pairs 1, 4, 6
 
 // P = 2^(S * scale_log2 - m) for NC keys of one row held in registers, packed
 // to bf16 pairs and stored over NC / 2 columns of the row's S in tensor
-// memory from s_addr; returns the sum (two lanes).  MIXED splits the
+// memory from s_addr; returns the sum (two lanes).  Once the first 64 keys'
+// P is stored the warp arrives on half_bar.  MIXED splits the
 // exponentials between MUFU and the polynomial; a partial last tile of a
 // document uses MUFU only, where a masked key (S = -inf) gives exactly 0.
 template <int NC, bool MIXED>
 __device__ __forceinline__ float2 softmax_exp_store(uint32_t (&sv)[NC], float scale_log2, float m,
-                                                    uint32_t s_addr) {
+                                                    uint32_t s_addr, uint32_t half_bar) {
   const float2 sc = make_float2(scale_log2, scale_log2);
   const float2 nm = make_float2(-m, -m);
   float2 acc0 = make_float2(0.f, 0.f), acc1 = make_float2(0.f, 0.f);
@@ -152,6 +156,13 @@ __device__ __forceinline__ float2 softmax_exp_store(uint32_t (&sv)[NC], float sc
       pk[c] = pack_bf16x2(e.x, e.y);
     }
     tmem_st_32x32b_x32(s_addr + h * 32, pk);
+    if (h == 0) {
+      // the first 64 keys of P are in TMEM: PV on them can start
+      tmem_st_wait();
+      tc_fence_before();
+      __syncwarp();
+      if ((threadIdx.x & 31) == 0) mbar_arrive(half_bar);
+    }
   }
   return add2(acc0, acc1);
 }
@@ -174,6 +185,7 @@ __global__ void __launch_bounds__(THREADS, 1) k_fmha(const __grid_constant__ Arg
   uint64_t* p_full = bars + 7;       // 2
   uint64_t* pv_done = bars + 9;      // 2
   uint64_t* drain = bars + 11;       // 1
+  uint64_t* p_half = bars + 12;      // 2: P of keys [0, 64) stored
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
@@ -200,6 +212,7 @@ __global__ void __launch_bounds__(THREADS, 1) k_fmha(const __grid_constant__ Arg
       mbar_init(smem_u32(&kv_empty[i]), 1);
       mbar_init(smem_u32(&s_full[i]), 1);
       mbar_init(smem_u32(&p_full[i]), 4);
+      mbar_init(smem_u32(&p_half[i]), 4);
       mbar_init(smem_u32(&pv_done[i]), 1);
     }
     mbar_init(smem_u32(drain), 1);
@@ -306,15 +319,28 @@ __global__ void __launch_bounds__(THREADS, 1) k_fmha(const __grid_constant__ Arg
         }
         tc_commit_elect(smem_u32(&s_full[t]));
       };
-      auto issue_pv = [&](int t, int j) {
+      auto issue_pv = [&](int t, int j, int half) {
         // 16 keys per MMA: P columns kk*8.. (bf16 pairs), V rows kk*16..
         // (MN-major: 64-dim chunks LBO = 16 KiB apart, 8-row groups SBO = 1 KiB)
         const uint64_t vd = smem_desc(smem_u32(smem + V_OFF + (j & 1) * TILE_BYTES), BOX_BYTES, 1024, 2);
 #pragma unroll
-        for (int kk = 0; kk < 8; ++kk)
+        for (int i = 0; i < 4; ++i) {
+          const int kk = half * 4 + i;
           tc_mma_bf16_ts_elect(tmem + o_col(t), tmem + s_col(t) + kk * 8, vd + kk * (2048 >> 4),
                                IDESC_PV, (j | kk) != 0);
-        if (j + 1 == n_kv) tc_commit_elect(smem_u32(&pv_done[t]));
+        }
+        if (half == 1 && j + 1 == n_kv) tc_commit_elect(smem_u32(&pv_done[t]));
+      };
+      // PV of tile t in two halves: keys [0, 64) once softmax has stored
+      // them, the rest once the whole P is in TMEM
+      auto pv_tile = [&](int t, int j) -> bool {
+        if (!wait(&p_half[t], j & 1)) return false;
+        tc_fence_after();
+        issue_pv(t, j, 0);
+        if (!wait(&p_full[t], j & 1)) return false;
+        tc_fence_after();
+        issue_pv(t, j, 1);
+        return true;
       };
       bool ok = wait(q_full, 0);
       if (ok) {
@@ -325,19 +351,15 @@ __global__ void __launch_bounds__(THREADS, 1) k_fmha(const __grid_constant__ Arg
       }
       for (int j = 0; j < n_kv && ok; ++j) {
         const bool more = j + 1 < n_kv;
-        if (!wait(&kv_full[j & 1], (j >> 1) & 1) || !wait(&p_full[0], j & 1)) {
+        if (!wait(&kv_full[j & 1], (j >> 1) & 1) || !pv_tile(0, j)) {
           ok = false;
           break;
         }
-        tc_fence_after();
-        issue_pv(0, j);
         if (more) issue_qk(0, j + 1);
-        if (!wait(&p_full[1], j & 1)) {
+        if (!pv_tile(1, j)) {
           ok = false;
           break;
         }
-        tc_fence_after();
-        issue_pv(1, j);
         if (more) issue_qk(1, j + 1);
         tc_commit_elect(smem_u32(&kv_empty[j & 1]));
       }
@@ -396,12 +418,10 @@ __global__ void __launch_bounds__(THREADS, 1) k_fmha(const __grid_constant__ Arg
         alpha = ex2(m_used - m_new);               // 0 on the first tile (m_used = -inf)
         m_used = m_new;
       }
-      // P written over the S columns already read
-      const float2 s2 = partial ? softmax_exp_store<128, false>(sv, p.scale_log2, m_used, s_t)
-                                : softmax_exp_store<128, true>(sv, p.scale_log2, m_used, s_t);
       if (rescale && j > 0) {
         // O is final for P(j-1): QK(j), whose completion s_full signalled, was
-        // issued after PV(j-1); PV(j) waits for p_full
+        // issued after PV(j-1); PV(j) waits for p_half, whose arrival follows
+        // these stores
 #pragma unroll
         for (int h = 0; h < 4; ++h) {
           uint32_t ov[32];
@@ -412,6 +432,10 @@ __global__ void __launch_bounds__(THREADS, 1) k_fmha(const __grid_constant__ Arg
           tmem_st_32x32b_x32(o_t + h * 32, ov);
         }
       }
+      // P written over the S columns already read
+      const uint32_t hb = smem_u32(&p_half[t]);
+      const float2 s2 = partial ? softmax_exp_store<128, false>(sv, p.scale_log2, m_used, s_t, hb)
+                                : softmax_exp_store<128, true>(sv, p.scale_log2, m_used, s_t, hb);
       l = l * alpha + (s2.x + s2.y);
       tmem_st_wait();
       tc_fence_before();
