@@ -116,6 +116,45 @@ def test_rmsnorm_modulated_and_long_rows(cuda):
 
 
 @pytest.mark.gpu
+@pytest.mark.parametrize("M,K,ldx,n_mod", [
+    (1, 256, 256, 2),          # one 256-column chunk, a single row
+    (257, 2048, 2048, 5),      # ragged last CTA, random modulation rows
+    (67, 3072, 3072, 0),       # the widest row held in registers by pass 1
+    (1000, 4096, 4160, 3),     # pass 1 re-reads the row; strided rows
+    (130, 4352, 4352, 0),
+])
+def test_rmsnorm_quantize_shapes(cuda, M, K, ldx, n_mod):
+    """Both pass-1 variants, row strides and modulation tables: y within 1e-2
+    of the oracle, the global scale = amax(y) / 2688 exactly, and the packed
+    bytes bit-exact against the oracle quantizer applied to the GPU's y."""
+    from h3_engine_b200 import ops
+    g = torch.Generator().manual_seed(M + K)
+    xw = torch.randn(M, ldx, generator=g).to(torch.bfloat16)
+    x = xw[:, :K]
+    gamma = (1 + 0.1 * torch.randn(K, generator=g)).to(torch.bfloat16)
+    kw = {}
+    mod = None
+    if n_mod:
+        shift = (0.1 * torch.randn(n_mod, K, generator=g)).to(torch.bfloat16)
+        scale = (0.1 * torch.randn(n_mod, K, generator=g)).to(torch.bfloat16)
+        idx = torch.randint(0, n_mod, (M,), generator=g, dtype=torch.int32)
+        kw = dict(shift=shift.to(cuda), scale=scale.to(cuda), mod_idx=idx.to(cuda))
+        mod = (shift.float().numpy(), scale.float().numpy(), idx.numpy())
+    xd = xw.to(cuda)[:, :K]
+    assert xd.stride(0) == ldx
+    q, sf, gs, y = ops.rmsnorm_quantize(xd, gamma.to(cuda), 1e-6, return_y=True, **kw)
+    torch.cuda.synchronize()
+    yg = y.float().cpu().numpy()
+    yr = B.rmsnorm(x.float().numpy(), gamma.float().numpy(), 1e-6, *(mod or ()))
+    assert R.max_rel_err(yg, yr) <= 1e-2
+    assert gs.item() == float(np.float32(np.abs(yg).max()) / np.float32(2688.0))
+    rq, rs, rgs = R.quantize(yg, mpad=q.shape[0])
+    assert gs.item() == float(rgs)
+    assert np.array_equal(q.cpu().numpy(), rq)
+    assert np.array_equal(sf.cpu().numpy(), R.swizzle(rs))
+
+
+@pytest.mark.gpu
 def test_ffn_block_full_size_row_sample(cuda):
     """The FFN sub-block at its configured size (32768 x 3072, FFN 12288): a
     row sample through the oracle, with the re-quantization global scale
