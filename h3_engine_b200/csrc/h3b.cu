@@ -176,12 +176,22 @@ int h3b_nvfp4_quantize(const void* x, int64_t M, int64_t K, int64_t ldx, const f
   auto xp = static_cast<const __nv_bfloat16*>(x);
   auto qp = static_cast<uint8_t*>(q);
   auto sp = static_cast<uint8_t*>(sf);
-  if (sf_layout == H3B_SF_SWIZZLED)
-    k_nvfp4_quantize<H3B_SF_SWIZZLED><<<(unsigned)blocks, kQuantThreads, 0, st>>>(
-        xp, M, K, ldx, amax, gs_in, gs_out, qp, sp, Mpad);
-  else
-    k_nvfp4_quantize<H3B_SF_ROWMAJOR><<<(unsigned)blocks, kQuantThreads, 0, st>>>(
-        xp, M, K, ldx, amax, gs_in, gs_out, qp, sp, Mpad);
+  const bool six = (K / 8) % (32 * 6) == 0;   // whole 6 x 256-element steps per row
+  if (sf_layout == H3B_SF_SWIZZLED) {
+    if (six)
+      k_nvfp4_quantize<H3B_SF_SWIZZLED, 6><<<(unsigned)blocks, kQuantThreads, 0, st>>>(
+          xp, M, K, ldx, amax, gs_in, gs_out, qp, sp, Mpad);
+    else
+      k_nvfp4_quantize<H3B_SF_SWIZZLED, 4><<<(unsigned)blocks, kQuantThreads, 0, st>>>(
+          xp, M, K, ldx, amax, gs_in, gs_out, qp, sp, Mpad);
+  } else {
+    if (six)
+      k_nvfp4_quantize<H3B_SF_ROWMAJOR, 6><<<(unsigned)blocks, kQuantThreads, 0, st>>>(
+          xp, M, K, ldx, amax, gs_in, gs_out, qp, sp, Mpad);
+    else
+      k_nvfp4_quantize<H3B_SF_ROWMAJOR, 4><<<(unsigned)blocks, kQuantThreads, 0, st>>>(
+          xp, M, K, ldx, amax, gs_in, gs_out, qp, sp, Mpad);
+  }
   return launched(cudaGetLastError());
 }
 

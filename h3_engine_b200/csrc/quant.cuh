@@ -101,13 +101,15 @@ __device__ __forceinline__ uint32_t quantize_half_block(const uint4& raw, float 
 }
 
 constexpr int kQuantThreads = 256;
-constexpr int kQuantUnroll = 4;
 
 // One warp per row (grid-stride over rows), two lanes per 16-element block,
-// each lane one 16-byte load; kQuantUnroll loads in flight per lane.  Reads
-// and code writes of a warp are contiguous 512-byte / 128-byte runs.  Rows
-// in [M, Mpad) are padding: they quantize zeros (codes and scales 0).
-template <int LAYOUT>
+// each lane one 16-byte load; UNROLL loads in flight per lane (6 where the
+// row is a whole number of 6 x 256-element steps, else 4: measured on the
+// DiT and FFN-hidden rows, 6 is 4 % faster there and slower where the last
+// step would be partly idle).  Reads and code writes of a warp are contiguous
+// 512-byte / 128-byte runs.  Rows in [M, Mpad) are padding: they quantize
+// zeros (codes and scales 0).
+template <int LAYOUT, int UNROLL>
 __global__ void __launch_bounds__(kQuantThreads)
     k_nvfp4_quantize(const __nv_bfloat16* __restrict__ x, int64_t M, int64_t K, int64_t ldx,
                      const float* __restrict__ amax, float gs_in, float* __restrict__ gs_out,
@@ -127,16 +129,16 @@ __global__ void __launch_bounds__(kQuantThreads)
     const bool real = r < M;
     const __nv_bfloat16* xr = x + r * ldx;
     uint8_t* qr = q + r * kq;
-    for (int h0 = 0; h0 < hpr; h0 += 32 * kQuantUnroll) {
-      uint4 raw[kQuantUnroll];
+    for (int h0 = 0; h0 < hpr; h0 += 32 * UNROLL) {
+      uint4 raw[UNROLL];
 #pragma unroll
-      for (int u = 0; u < kQuantUnroll; ++u) {
+      for (int u = 0; u < UNROLL; ++u) {
         const int h = h0 + u * 32 + lane;
         raw[u] = make_uint4(0, 0, 0, 0);
         if (real && h < hpr) raw[u] = ld_nc_v4(xr + (int64_t)h * 8);
       }
 #pragma unroll
-      for (int u = 0; u < kQuantUnroll; ++u) {
+      for (int u = 0; u < UNROLL; ++u) {
         const int h = h0 + u * 32 + lane;
         uint32_t s8;
         const uint32_t packed = quantize_half_block(raw[u], gs, d6, s8);
