@@ -71,13 +71,31 @@ __device__ __forceinline__ int64_t sf_swizzled_offset(int64_t r, int64_t c, int6
   return ((r >> 7) * c4 + (c >> 2)) * 512 + (r & 31) * 16 + ((r & 127) >> 5) * 4 + (c & 3);
 }
 
+// Per-tensor table of the reciprocal each block multiplies by: entry s holds
+// __frcp_rn(d) with d = float(s) * gs, or 0 where d == 0 (the block's codes
+// are then all +0).  A block scale is never negative (it is the saturating
+// e4m3 conversion of |x|max / (6 gs) >= 0), so its byte indexes 128 entries.
+// Each CTA of a quantizing kernel fills its own copy in shared memory once:
+// 128 reciprocals instead of one decode, multiply and IEEE reciprocal per
+// 16-element block.
+constexpr int kInvTableSize = 128;
+
+__device__ __forceinline__ void fill_inv_table(float* tab, float gs) {
+  for (int s = threadIdx.x; s < kInvTableSize; s += blockDim.x) {
+    const float d = __fmul_rn(e4m3_to_f32_hw((uint32_t)s), gs);
+    tab[s] = d != 0.f ? __frcp_rn(d) : 0.f;
+  }
+  __syncthreads();
+}
+
 // Quantize 8 consecutive bf16 values (one lane's half of a 16-block; the
 // partner half sits in the neighbouring lane).  Returns 4 packed code bytes
 // and the block's scale byte.  The block max is taken on the bf16 bit
 // patterns: |x| of a bf16 is its bits & 0x7FFF, and non-negative bf16 values
 // order like their 16-bit integers (NaN inputs are outside the recipe).
-__device__ __forceinline__ uint32_t quantize_half_block(const uint4& raw, float gs, float d6,
-                                                        uint32_t& s8_out) {
+// inv_tab: the tensor's reciprocal table (fill_inv_table).
+__device__ __forceinline__ uint32_t quantize_half_block(const uint4& raw, const float* inv_tab,
+                                                        float d6, uint32_t& s8_out) {
   const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
   uint32_t m2 = __vmaxu2(w[0] & 0x7FFF7FFFu, w[1] & 0x7FFF7FFFu);
   m2 = __vmaxu2(m2, __vmaxu2(w[2] & 0x7FFF7FFFu, w[3] & 0x7FFF7FFFu));
@@ -85,10 +103,9 @@ __device__ __forceinline__ uint32_t quantize_half_block(const uint4& raw, float 
   mb = max(mb, __shfl_xor_sync(0xffffffffu, mb, 1));
   const float m = __uint_as_float(mb << 16);
   const uint32_t s8 = f32_to_e4m3_sat(__fdiv_rn(m, d6));
-  const float d = __fmul_rn(e4m3_to_f32_hw(s8), gs);
+  const float inv = inv_tab[s8 & (kInvTableSize - 1)];
   uint32_t packed = 0;
-  if (d != 0.f) {
-    const float inv = __frcp_rn(d);
+  if (inv != 0.f) {
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
       float a, b;
@@ -117,6 +134,8 @@ __global__ void __launch_bounds__(kQuantThreads)
   const float gs = amax ? global_scale_from_amax(__ldg(amax)) : gs_in;
   const float d6 = __fmul_rn(6.0f, gs);
   if (gs_out != nullptr && blockIdx.x == 0 && threadIdx.x == 0) *gs_out = gs;
+  __shared__ float inv_tab[kInvTableSize];
+  fill_inv_table(inv_tab, gs);
 
   const int lane = threadIdx.x & 31;
   const int hpr = (int)(K >> 3);              // 8-element halves per row (even)
@@ -141,7 +160,7 @@ __global__ void __launch_bounds__(kQuantThreads)
       for (int u = 0; u < UNROLL; ++u) {
         const int h = h0 + u * 32 + lane;
         uint32_t s8;
-        const uint32_t packed = quantize_half_block(raw[u], gs, d6, s8);
+        const uint32_t packed = quantize_half_block(raw[u], inv_tab, d6, s8);
         if (h < hpr) {
           *reinterpret_cast<uint32_t*>(qr + (int64_t)h * 4) = packed;
           if ((lane & 1) == 0) {
