@@ -269,11 +269,19 @@ class AttentionWorkload:
         self.rank_gemm_flops = 0
         self.rank_attn_flops = fl
         self.events = None
-        self.config = {"workload": "packed varlen attention (bf16 q|k|v activation, 24 heads x 128, "
-                                   "one softmax(QK^T / sqrt(d)) V per document)",
-                       "documents": self.cu, "heads": H, "head_dim": D,
-                       "parallelism": f"replicas x{world}",
-                       "l2": f"q|k|v {self.qkv.numel() * 2 / 1e6:.0f} MB per launch"}
+        self.config = self.describe(world, docs)
+
+    @classmethod
+    def describe(cls, world: int, docs: list[int]) -> dict:
+        cu = [0]
+        for n in docs:
+            cu.append(cu[-1] + n)
+        qkv_mb = cu[-1] * 3 * cls.HEADS * cls.HEAD_DIM * 2 / 1e6
+        return {"workload": "packed varlen attention (bf16 q|k|v activation, 24 heads x 128, "
+                            "one softmax(QK^T / sqrt(d)) V per document)",
+                "documents": cu, "heads": cls.HEADS, "head_dim": cls.HEAD_DIM,
+                "parallelism": f"replicas x{world}",
+                "l2": f"q|k|v {qkv_mb:.0f} MB per launch"}
 
     def set_timers(self, gemm, attn):
         self.events = attn
@@ -524,32 +532,112 @@ def cpu_ffn_run(sample_tokens: int, min_seconds: float = CPU_SAMPLE_SECONDS) -> 
                        f"{dt * n:.1f} s of CPU work")}
 
 
+def cpu_quant_run(sample_rows: int, min_seconds: float = CPU_SAMPLE_SECONDS) -> dict:
+    """The quantize microbenchmark on the CPU port: amax + NVFP4 quantization
+    of ``sample_rows`` rows of each of its four shapes (same value
+    distribution), repeated for ``min_seconds``; GB/s of the 4.5625 algorithmic
+    bytes per element, the unit of the GPU line."""
+    from oracle.cpu_torch import quantize
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    g = torch.Generator().manual_seed(1)
+    xs = []
+    for _, K in QuantWorkload.SHAPES:
+        x = torch.randn(sample_rows, K, generator=g)
+        hot = torch.rand(sample_rows, K, generator=g) < 1e-3
+        xs.append(torch.where(hot, x * 50, x).to(torch.bfloat16))
+
+    def run():
+        for x in xs:
+            quantize(x)                   # amax of the sample, then codes and scales
+
+    dt, n = _timed_repeat(run, min_seconds)
+    sample_elems = sum(x.numel() for x in xs)
+    full_elems = sum(M * K for M, K in QuantWorkload.SHAPES)
+    return {"value": 4.5625 * sample_elems / dt / 1e9, "unit": "GB/s",
+            "cores": torch.get_num_threads(), "kind": "port",
+            "s_per_step": dt * full_elems / sample_elems,
+            "sample": (f"{sample_rows} rows of each of the 4 shapes x {n} repeats, "
+                       f"{dt * n:.1f} s of CPU work")}
+
+
+def cpu_attention_run(docs: list[int], sample_rows: int,
+                      min_seconds: float = CPU_SAMPLE_SECONDS) -> dict:
+    """Packed attention on the CPU: softmax(Q K^T / sqrt(d)) V in fp32 torch
+    ops for ``sample_rows`` query rows of each document against all of that
+    document's keys (24 heads x 128), repeated for ``min_seconds``; TFLOP/s of
+    4 * H * D * rows * keys, scaled to every query row for ms_per_step."""
+    H, D = AttentionWorkload.HEADS, AttentionWorkload.HEAD_DIM
+    torch.set_num_threads(os.cpu_count() or 1)
+    g = torch.Generator().manual_seed(3)
+    parts = []
+    for n in docs:
+        rows = min(sample_rows, n)
+        q = torch.randn(H, rows, D, generator=g).to(torch.bfloat16).float()
+        k = torch.randn(H, n, D, generator=g).to(torch.bfloat16).float()
+        v = torch.randn(H, n, D, generator=g).to(torch.bfloat16).float()
+        parts.append((q, k, v))
+
+    def run():
+        for q, k, v in parts:
+            p = torch.softmax(q @ k.transpose(1, 2) * D ** -0.5, dim=-1)
+            (p @ v).to(torch.bfloat16)
+
+    dt, n_rep = _timed_repeat(run, min_seconds)
+    sample_flops = sum(4 * H * D * q.shape[1] * k.shape[1] for q, k, _ in parts)
+    full_flops = sum(4 * H * D * n * n for n in docs)
+    return {"value": sample_flops / dt / 1e12, "unit": "TFLOP/s",
+            "cores": torch.get_num_threads(), "kind": "port",
+            "s_per_step": dt * full_flops / sample_flops,
+            "sample": (f"{sample_rows} query rows per document x all its keys, {n_rep} repeats, "
+                       f"{dt * n_rep:.1f} s of CPU work")}
+
+
+def cpu_baseline_run(args) -> dict | None:
+    """The CPU arm of ``args.workload`` (None where it has none)."""
+    if args.workload == "dit":
+        return cpu_dit_estimate(args.cpu_rows, args.cpu_seconds)
+    if args.workload == "ffn":
+        return cpu_ffn_run(args.cpu_rows, args.cpu_seconds)
+    if args.workload == "quant":
+        return cpu_quant_run(args.cpu_rows, args.cpu_seconds)
+    if args.workload == "attention":
+        return cpu_attention_run([int(n) for n in args.attn_docs.split(",")], args.cpu_rows,
+                                 args.cpu_seconds)
+    return None
+
+
 def run_reference(args) -> None:
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
-    if args.workload in ("attention", "refblock", "quant"):
-        print(json.dumps({"impl": "reference", "unavailable": f"the {args.workload} profiling "
-                          "workload has no CPU arm; the dit and ffn workloads have one"}), flush=True)
+    if args.workload == "refblock":
+        print(json.dumps({"impl": "reference", "unavailable": "the reference-shape block "
+                          "(hidden 5376, SwiGLU) has no CPU arm; the dit, ffn, attention and "
+                          "quant workloads have one"}), flush=True)
         return
-    vals = []
-    for _ in range(max(args.steps, 1)):
-        r = cpu_dit_estimate(args.cpu_rows, args.cpu_seconds) if args.workload == "dit" else cpu_ffn_run(args.cpu_rows, args.cpu_seconds)
-        vals.append(r)
+    vals = [cpu_baseline_run(args) for _ in range(max(args.steps, 1))]
     v = statistics.median([r["value"] for r in vals])
     r = vals[-1]
+    unit = r["unit"]
+    configs = {"dit": lambda: DiTWorkload.describe(args.gpus),
+               "ffn": lambda: FFNWorkload.describe(args.gpus),
+               "quant": lambda: QuantWorkload.describe(args.gpus),
+               "attention": lambda: AttentionWorkload.describe(
+                   args.gpus, [int(n) for n in args.attn_docs.split(",")])}
+    dtypes = {"dit": "fp32 (NVFP4 operands decoded)", "ffn": "fp32 (NVFP4 operands decoded)",
+              "quant": "fp32 -> e2m1 / e4m3", "attention": "fp32 (bf16 q|k|v)"}
     line = {
-        "impl": "reference", "metric": METRIC, "value": v, "unit": "TFLOP/s",
+        "impl": "reference", "metric": METRIC, "value": v, "unit": unit,
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": statistics.median([x["s_per_step"] for x in vals]) * 1e3,
         "higher_is_better": True, "scaling": "strong" if args.workload == "dit" else "weak",
-        "vs_baseline": None, "dtype": "fp32 (NVFP4 operands decoded)",
+        "vs_baseline": None, "dtype": dtypes[args.workload],
         "data": "synthetic",
-        "config": (DiTWorkload.describe(args.gpus) if args.workload == "dit"
-                   else FFNWorkload.describe(args.gpus)),
-        "cpu_baseline": {"value": v, "unit": "TFLOP/s", "cores": r["cores"], "kind": r["kind"],
+        "config": configs[args.workload](),
+        "cpu_baseline": {"value": v, "unit": unit, "cores": r["cores"], "kind": r["kind"],
                          "sample": r["sample"]},
-        "e2e": {"value": v, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "e2e": {"value": v, "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
 
@@ -634,9 +722,8 @@ def run_ours(args) -> None:
         extras["cuda_graph"] = graph_step_timing(wl, args.steps)
     if rank == 0 and not args.no_extras:
         extras["library_gemm_torch_scaled_mm"] = library_gemm_reference(dev)
-        if world == 1 and args.workload in ("dit", "ffn"):
-            cpu = (cpu_dit_estimate(args.cpu_rows, args.cpu_seconds) if args.workload == "dit"
-                   else cpu_ffn_run(args.cpu_rows, args.cpu_seconds))
+        cpu = cpu_baseline_run(args) if world == 1 else None
+        if cpu is not None:
             extras["cpu_baseline"] = {k: cpu[k] for k in ("value", "unit", "cores", "kind", "sample")}
 
     if rank == 0:
