@@ -25,7 +25,7 @@ def flags(monkeypatch):
 
 
 def rel(a, b):
-    a, b = a.float(), b.float()
+    a, b = a.detach().float(), b.detach().float()
     return float((a - b).abs().max() / b.abs().max())
 
 
