@@ -25,7 +25,7 @@ mask, head_dim other than 128 for attention, rotary widths whose half is not
 a multiple of 8, ...) is MISS, on which the shims run the reference's stock
 torch expression, as the reference does.  A covered call never falls back:
 a missing libh3b.so or a failing launch raises.  ``miss_counts()`` reports
-the MISSes per name.
+the MISSes per name (of ``try_call`` and of the armed shims).
 """
 from __future__ import annotations
 
@@ -85,11 +85,16 @@ def _table():
     }
 
 
+def note_miss(name: str) -> None:
+    """Count an armed call the kernels did not take (the shims call this too)."""
+    _MISSED[name] = _MISSED.get(name, 0) + 1
+
+
 def try_call(name: str, *args, **kwargs):
     fn = _table().get(name)
     out = MISS if fn is None else fn(*args, **kwargs)
     if out is MISS:
-        _MISSED[name] = _MISSED.get(name, 0) + 1
+        note_miss(name)
     return out
 
 

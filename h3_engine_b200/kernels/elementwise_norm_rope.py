@@ -23,7 +23,7 @@ from __future__ import annotations
 import torch
 from torch import nn
 
-from h3_engine_b200.kernels._dispatch import MISS, enabled
+from h3_engine_b200.kernels._dispatch import MISS, enabled, note_miss
 
 
 def rms_norm(norm_module: nn.RMSNorm, x: torch.Tensor) -> torch.Tensor:
@@ -68,6 +68,7 @@ def apply_rotary_emb(hidden_states: torch.Tensor, cos: torch.Tensor, sin: torch.
         out = rope_kernel(hidden_states, None, 0.0, cos, sin)
         if out is not MISS:
             return out
+        note_miss("rope")
     rotary_dim = cos.shape[-1]
     rot, rest = hidden_states[..., :rotary_dim], hidden_states[..., rotary_dim:]
     c = cos.to(hidden_states.dtype)[None, :, None, :]
@@ -127,6 +128,7 @@ def norm_modulate(norm_module: nn.RMSNorm, x: torch.Tensor, scale: torch.Tensor,
     out = norm_modulate_kernel(x, w, float(norm_module.eps), scale, shift, indices)
     if out is not MISS:
         return out
+    note_miss("norm_modulate_h3")
     return _norm_modulate_impl(x, w, float(norm_module.eps), scale, shift, indices)
 
 
@@ -159,6 +161,7 @@ def norm_rope(norm_module: nn.RMSNorm, x: torch.Tensor, cos: torch.Tensor,
     out = rope_kernel(x, w, float(norm_module.eps), cos, sin)
     if out is not MISS:
         return out
+    note_miss("norm_rope_h3")
     return _norm_rope_impl(x, w, float(norm_module.eps), cos, sin)
 
 

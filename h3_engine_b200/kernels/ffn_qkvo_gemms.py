@@ -21,7 +21,7 @@ from __future__ import annotations
 import torch
 from torch import nn
 
-from h3_engine_b200.kernels._dispatch import MISS, enabled
+from h3_engine_b200.kernels._dispatch import MISS, enabled, note_miss
 
 
 def qkv_kernel(to_q, to_k, to_v, x: torch.Tensor):
@@ -96,6 +96,7 @@ def qkv_projection(to_q: nn.Linear, to_k: nn.Linear, to_v: nn.Linear,
         out = qkv_kernel(to_q, to_k, to_v, x)
         if out is not MISS:
             return out
+        note_miss("qkv_projection")
     return to_q(x), to_k(x), to_v(x)
 
 
@@ -104,6 +105,7 @@ def out_projection(to_out: nn.Linear, x: torch.Tensor) -> torch.Tensor:
         out = out_kernel(to_out, x)
         if out is not MISS:
             return out
+        note_miss("out_projection")
     return to_out(x)
 
 
@@ -123,6 +125,7 @@ def ffn(ff: nn.Module, x: torch.Tensor) -> torch.Tensor:
         out = ffn_kernel(ff, x)
         if out is not MISS:
             return out
+        note_miss("ffn")
     if enabled("H3_FUSED_SWIGLU"):
         return ff.net[2](_swiglu(ff.net[0].proj(x)))
     return ff(x)

@@ -12,7 +12,7 @@ from __future__ import annotations
 import torch
 import torch.nn.functional as F
 
-from h3_engine_b200.kernels._dispatch import MISS, enabled
+from h3_engine_b200.kernels._dispatch import MISS, enabled, note_miss
 
 _MAX_DOCS = 64
 
@@ -58,6 +58,7 @@ def packed_self_attention(query: torch.Tensor, key: torch.Tensor, value: torch.T
         out = attention_kernel(query, key, value)
         if out is not MISS:
             return out
+        note_miss("attention")
     out = F.scaled_dot_product_attention(query.transpose(1, 2), key.transpose(1, 2),
                                          value.transpose(1, 2), attn_mask=attention_mask,
                                          dropout_p=0.0, is_causal=False)
