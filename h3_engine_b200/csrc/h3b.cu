@@ -176,21 +176,22 @@ int h3b_nvfp4_quantize(const void* x, int64_t M, int64_t K, int64_t ldx, const f
   auto xp = static_cast<const __nv_bfloat16*>(x);
   auto qp = static_cast<uint8_t*>(q);
   auto sp = static_cast<uint8_t*>(sf);
-  const bool six = (K / 8) % (32 * 6) == 0;   // whole 6 x 256-element steps per row
+  // loads in flight per lane: 6 or 7 where a row is a whole number of such
+  // steps (32 lanes x 8 values each), else 4
+  const int64_t hpr = K / 8;
+  const int unroll = hpr % (32 * 6) == 0 ? 6 : hpr % (32 * 7) == 0 ? 7 : 4;
+  auto launch = [&](auto kernel) {
+    kernel<<<(unsigned)blocks, kQuantThreads, 0, st>>>(xp, M, K, ldx, amax, gs_in, gs_out, qp,
+                                                       sp, Mpad);
+  };
   if (sf_layout == H3B_SF_SWIZZLED) {
-    if (six)
-      k_nvfp4_quantize<H3B_SF_SWIZZLED, 6><<<(unsigned)blocks, kQuantThreads, 0, st>>>(
-          xp, M, K, ldx, amax, gs_in, gs_out, qp, sp, Mpad);
-    else
-      k_nvfp4_quantize<H3B_SF_SWIZZLED, 4><<<(unsigned)blocks, kQuantThreads, 0, st>>>(
-          xp, M, K, ldx, amax, gs_in, gs_out, qp, sp, Mpad);
+    if (unroll == 6) launch(k_nvfp4_quantize<H3B_SF_SWIZZLED, 6>);
+    else if (unroll == 7) launch(k_nvfp4_quantize<H3B_SF_SWIZZLED, 7>);
+    else launch(k_nvfp4_quantize<H3B_SF_SWIZZLED, 4>);
   } else {
-    if (six)
-      k_nvfp4_quantize<H3B_SF_ROWMAJOR, 6><<<(unsigned)blocks, kQuantThreads, 0, st>>>(
-          xp, M, K, ldx, amax, gs_in, gs_out, qp, sp, Mpad);
-    else
-      k_nvfp4_quantize<H3B_SF_ROWMAJOR, 4><<<(unsigned)blocks, kQuantThreads, 0, st>>>(
-          xp, M, K, ldx, amax, gs_in, gs_out, qp, sp, Mpad);
+    if (unroll == 6) launch(k_nvfp4_quantize<H3B_SF_ROWMAJOR, 6>);
+    else if (unroll == 7) launch(k_nvfp4_quantize<H3B_SF_ROWMAJOR, 7>);
+    else launch(k_nvfp4_quantize<H3B_SF_ROWMAJOR, 4>);
   }
   return launched(cudaGetLastError());
 }
@@ -400,10 +401,16 @@ int h3b_qk_norm_rope(void* q, int64_t q_stride, int64_t q_off, void* k, int64_t 
   const int64_t cap = (int64_t)num_sms() * 8;
   if (blocks > cap) blocks = cap;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  if (D == 128)
-    k_qk_norm_rope<128><<<(unsigned)blocks, kRopeWarps * 32, 0, st>>>(a);
-  else
-    k_qk_norm_rope<64><<<(unsigned)blocks, kRopeWarps * 32, 0, st>>>(a);
+  // head vectors of a row per warp instruction: 32 lanes / (D / 8 lanes each)
+  const int steps = (a.hq + a.hk) / (256 / D);
+  const bool seven = steps % 6 != 0 && steps % 7 == 0;
+  if (D == 128) {
+    if (seven) k_qk_norm_rope<128, 7><<<(unsigned)blocks, kRopeWarps * 32, 0, st>>>(a);
+    else k_qk_norm_rope<128, 6><<<(unsigned)blocks, kRopeWarps * 32, 0, st>>>(a);
+  } else {
+    if (seven) k_qk_norm_rope<64, 7><<<(unsigned)blocks, kRopeWarps * 32, 0, st>>>(a);
+    else k_qk_norm_rope<64, 6><<<(unsigned)blocks, kRopeWarps * 32, 0, st>>>(a);
+  }
   return launched(cudaGetLastError());
 }
 

@@ -120,10 +120,10 @@ __device__ __forceinline__ uint32_t quantize_half_block(const uint4& raw, const 
 constexpr int kQuantThreads = 256;
 
 // One warp per row (grid-stride over rows), two lanes per 16-element block,
-// each lane one 16-byte load; UNROLL loads in flight per lane (6 where the
-// row is a whole number of 6 x 256-element steps, else 4: measured on the
-// DiT and FFN-hidden rows, 6 is 4 % faster there and slower where the last
-// step would be partly idle).  Reads and code writes of a warp are contiguous
+// each lane one 16-byte load; UNROLL loads in flight per lane (6 or 7 where
+// the row is a whole number of such steps of 32 loads, else 4: measured on
+// the DiT and FFN-hidden rows, 6 is 4 % faster there and slower where the
+// last step would be partly idle).  Reads and code writes of a warp are contiguous
 // 512-byte / 128-byte runs.  Rows in [M, Mpad) are padding: they quantize
 // zeros (codes and scales 0).
 template <int LAYOUT, int UNROLL>

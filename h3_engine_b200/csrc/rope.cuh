@@ -36,10 +36,11 @@ struct RopeArgs {
 };
 
 constexpr int kRopeWarps = 8;
-// 16-byte loads in flight per lane: 6 (12 head vectors of 128 per warp
-// iteration, 116 registers, 2 CTAs per SM) measured 10 % faster than 4 on the
-// DiT rows (24 + 24 heads); 8 and 12 drop to one CTA per SM and are slower.
-constexpr int kRopeUnroll = 6;
+// 16-byte loads in flight per lane (UNROLL): 6 (12 head vectors of 128 per
+// warp iteration, 2 CTAs per SM) measured 10 % faster than 4 on the DiT rows
+// (24 + 24 heads); 8 and 12 drop to one CTA per SM and are slower.  The host
+// takes 7 where a row's head vectors are a whole number of 7-deep steps and
+// not of 6-deep ones (56 + 56 heads), so no step runs partly idle.
 
 // One warp per token row (grid-stride over rows).  A head vector of D values
 // is spread over LPH = D/8 lanes, 8 consecutive values (one 16-byte load) per
@@ -49,7 +50,7 @@ constexpr int kRopeUnroll = 6;
 // warp.  The sum of squares reduces over the LPH lanes of a head; the
 // rotate-half partner of column j (j +- R/2, R/2 a multiple of 8) is the
 // lane (R/2)/8 away in the same head, fetched with shuffles.
-template <int D>
+template <int D, int UNROLL>
 __global__ void __launch_bounds__(kRopeWarps * 32) k_qk_norm_rope(const RopeArgs a) {
   constexpr int LPH = D / 8;                 // lanes per head vector
   constexpr int HPW = 32 / LPH;              // head vectors per warp instruction
@@ -84,12 +85,12 @@ __global__ void __launch_bounds__(kRopeWarps * 32) k_qk_norm_rope(const RopeArgs
     }
     __nv_bfloat16* qrow = a.hq ? a.q + t * a.q_stride + a.q_off : nullptr;
     __nv_bfloat16* krow = a.hk ? a.k + t * a.k_stride + a.k_off : nullptr;
-    for (int v0 = 0; v0 < nv; v0 += HPW * kRopeUnroll) {
-      uint4 raw[kRopeUnroll];
-      __nv_bfloat16* ptr[kRopeUnroll];
-      bool is_k[kRopeUnroll], valid[kRopeUnroll];
+    for (int v0 = 0; v0 < nv; v0 += HPW * UNROLL) {
+      uint4 raw[UNROLL];
+      __nv_bfloat16* ptr[UNROLL];
+      bool is_k[UNROLL], valid[UNROLL];
 #pragma unroll
-      for (int u = 0; u < kRopeUnroll; ++u) {
+      for (int u = 0; u < UNROLL; ++u) {
         const int v = v0 + u * HPW + lane / LPH;
         valid[u] = v < nv;
         is_k[u] = v >= a.hq;
@@ -98,7 +99,7 @@ __global__ void __launch_bounds__(kRopeWarps * 32) k_qk_norm_rope(const RopeArgs
         raw[u] = valid[u] ? *reinterpret_cast<const uint4*>(ptr[u]) : make_uint4(0, 0, 0, 0);
       }
 #pragma unroll
-      for (int u = 0; u < kRopeUnroll; ++u) {
+      for (int u = 0; u < UNROLL; ++u) {
         const uint32_t w[4] = {raw[u].x, raw[u].y, raw[u].z, raw[u].w};
         float x[8];
 #pragma unroll
