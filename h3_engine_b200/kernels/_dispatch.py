@@ -70,11 +70,17 @@ def miss_counts(reset: bool = False) -> dict[str, int]:
     return out
 
 
-def _table():
+_TABLE: dict | None = None
+
+
+def _table() -> dict:
+    global _TABLE
+    if _TABLE is not None:
+        return _TABLE
     from h3_engine_b200.kernels import elementwise_norm_rope as ew
     from h3_engine_b200.kernels import ffn_qkvo_gemms as gm
     from h3_engine_b200.kernels import packed_self_attn as at
-    return {
+    _TABLE = {
         "rope": lambda x, cos, sin: ew.rope_kernel(x, None, 0.0, cos, sin),
         "norm_rope_h3": ew.rope_kernel,
         "norm_modulate_h3": ew.norm_modulate_kernel,
@@ -83,6 +89,7 @@ def _table():
         "out_projection": gm.out_kernel,
         "ffn": gm.ffn_kernel,
     }
+    return _TABLE
 
 
 def note_miss(name: str) -> None:
