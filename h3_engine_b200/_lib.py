@@ -46,6 +46,7 @@ SIGNATURES: dict[str, tuple] = {
     "h3b_rmsnorm_quantize_noalloc": (_i32, [_c_void_p, _i64, _i64, _i64, _c_void_p, _f32,
                                             _c_void_p, _c_void_p, _c_void_p, _c_void_p,
                                             _c_void_p, _c_void_p, _i64, _c_void_p]),
+    "h3b_selftest_bounded_wait": (_i32, [_i64, _c_void_p]),
 }
 
 _lock = threading.Lock()

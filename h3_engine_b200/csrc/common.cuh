@@ -131,16 +131,35 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
 // Bounded wait for the phase of `bar` with parity `parity` to complete.
 // Returns false when `abort` was raised by another role or the time limit
 // passed; the caller then records an error and unwinds.
-__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort) {
+__device__ __forceinline__ bool mbar_wait_for(uint32_t bar, uint32_t parity, volatile int* abort,
+                                              uint64_t limit_ns) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer();
   for (uint32_t i = 1;; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
     if ((i & 63u) == 0) {
       if (abort != nullptr && *abort) return false;
-      if (globaltimer() - t0 > kWaitLimitNs) return false;
+      if (globaltimer() - t0 > limit_ns) return false;
     }
   }
+}
+
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort) {
+  return mbar_wait_for(bar, parity, abort, kWaitLimitNs);
+}
+
+// Self-test of the bounded wait (h3b_selftest_bounded_wait): a barrier that
+// nothing arrives on; the wait expires after limit_ns, the kernel records
+// H3B_ERR_TIMEOUT and returns.
+__global__ void k_selftest_bounded_wait(uint64_t limit_ns) {
+  __shared__ __align__(8) uint64_t bar;
+  if (threadIdx.x == 0) {
+    mbar_init(smem_u32(&bar), 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+  const bool ok = mbar_wait_for(smem_u32(&bar), 0, nullptr, limit_ns);
+  if (!ok && threadIdx.x == 0) record_error(H3B_ERR_TIMEOUT);
 }
 
 // ---------------------------------------------------------------- TMA / bulk copies

@@ -552,6 +552,15 @@ static int noalloc_scratch(float** out) {
 }
 }  // namespace h3b
 
+int h3b_selftest_bounded_wait(int64_t limit_us, void* stream) {
+  if (limit_us < 1 || limit_us > 1000000) return H3B_ERR_INVALID_ARG;
+  int rc = check_sm100();
+  if (rc != H3B_OK) return rc;
+  k_selftest_bounded_wait<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(
+      (uint64_t)limit_us * 1000ull);
+  return launched(cudaGetLastError());
+}
+
 int h3b_rmsnorm_quantize_noalloc(const void* x, int64_t M, int64_t K, int64_t ldx,
                                  const void* gamma, float eps, const void* shift,
                                  const void* scale, const int32_t* mod_idx, float* gs_out,

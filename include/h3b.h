@@ -201,6 +201,15 @@ H3B_API int h3b_rmsnorm_quantize_noalloc(const void* x, int64_t M, int64_t K, in
                                          float* gs_out, void* q, void* sf, int64_t Mpad,
                                          void* stream);
 
+/* Self-test of the failure path every kernel above shares (no reference
+ * counterpart): one CTA waits, with the kernels' bounded mbarrier wait but a
+ * bound of limit_us microseconds, on a barrier that nothing arrives on; when
+ * the bound expires it records H3B_ERR_TIMEOUT in the device error word and
+ * returns, as the GEMM and attention kernels do when a pipeline stage never
+ * completes.  The context stays usable; read and clear the word with
+ * h3b_device_error.  1 <= limit_us <= 1000000, else H3B_ERR_INVALID_ARG.    */
+H3B_API int h3b_selftest_bounded_wait(int64_t limit_us, void* stream);
+
 #ifdef __cplusplus
 }
 #endif
