@@ -353,11 +353,21 @@ class RefBlockWorkload:
         self.rope = rope_tables(pos, reference_dims(16), 10000.0)
         self.x = torch.randn(T, C, generator=g, device=dev).to(torch.bfloat16)
         self.y = torch.empty_like(self.x)
-        self.rank_gemm_flops = 2 * T * C * 3 * HD + 2 * T * HD * C + 2 * T * C * 2 * F + 2 * T * F * C
+        self.rank_gemm_flops = self.gemm_flops()
         self.rank_attn_flops = 4 * HD * T * T
         self.step_flops = world * (self.rank_gemm_flops + self.rank_attn_flops)
         self.attn_traffic = T * (3 * HD * 2 + HD * 2)    # q|k|v read once, O written
         self.config = self.describe(world)
+
+    @classmethod
+    def gemm_flops(cls) -> int:
+        C, HD, F, T = cls.C, cls.H * cls.D, cls.F, cls.TOKENS
+        return 2 * T * C * 3 * HD + 2 * T * HD * C + 2 * T * C * 2 * F + 2 * T * F * C
+
+    @classmethod
+    def flops(cls) -> int:
+        """NVFP4 GEMM + attention flops of one block."""
+        return cls.gemm_flops() + 4 * cls.H * cls.D * cls.TOKENS * cls.TOKENS
 
     @classmethod
     def describe(cls, world: int) -> dict:
@@ -593,6 +603,32 @@ def cpu_attention_run(docs: list[int], sample_rows: int,
                        f"{dt * n_rep:.1f} s of CPU work")}
 
 
+def cpu_refblock_run(sample_rows: int, min_seconds: float = CPU_SAMPLE_SECONDS) -> dict:
+    """The reference-shape block on the CPU port: attention half (sample rows
+    against all 38247 keys, 56 x 128 heads) and SwiGLU FFN half on
+    ``sample_rows`` rows, repeated for ``min_seconds``, scaled to every row."""
+    from h3_engine_b200.rope import reference_dims, rope_tables
+    from oracle.cpu_torch import AttnRowsCPU, FFNBlockCPU
+
+    W = RefBlockWorkload
+    torch.set_num_threads(os.cpu_count() or 1)
+    attn = AttnRowsCPU(W.C, W.H, W.D, W.TOKENS, seed=5)
+    g = torch.Generator().manual_seed(5)
+    w = lambda n, k: (torch.randn(n, k, generator=g) / k ** 0.5).to(torch.bfloat16)  # noqa: E731
+    ffn = FFNBlockCPU(w(2 * W.F, W.C), None, w(W.C, W.F), None, torch.ones(W.C), 1e-5,
+                      act="swiglu")
+    x = torch.randn(sample_rows, W.C, generator=g).to(torch.bfloat16)
+    pos = torch.randint(0, 32, (sample_rows, 3), generator=g).float()
+    cos, sin = rope_tables(pos, reference_dims(16), 10000.0)
+    dt, n = _timed_repeat(lambda: ffn(attn(x, cos, sin)), min_seconds)
+    step_s = dt * W.TOKENS / sample_rows
+    return {"value": W.flops() / step_s / 1e12, "unit": "TFLOP/s",
+            "cores": torch.get_num_threads(), "kind": "port", "s_per_step": step_s,
+            "sample": (f"{sample_rows} of {W.TOKENS} rows (attention against all keys + SwiGLU "
+                       f"FFN) x {n} repeats, {dt * n:.1f} s of CPU work, extrapolated "
+                       f"linearly to every row")}
+
+
 def cpu_baseline_run(args) -> dict | None:
     """The CPU arm of ``args.workload`` (None where it has none)."""
     if args.workload == "dit":
@@ -604,17 +640,14 @@ def cpu_baseline_run(args) -> dict | None:
     if args.workload == "attention":
         return cpu_attention_run([int(n) for n in args.attn_docs.split(",")], args.cpu_rows,
                                  args.cpu_seconds)
+    if args.workload == "refblock":
+        return cpu_refblock_run(args.cpu_rows, args.cpu_seconds)
     return None
 
 
 def run_reference(args) -> None:
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
-        return
-    if args.workload == "refblock":
-        print(json.dumps({"impl": "reference", "unavailable": "the reference-shape block "
-                          "(hidden 5376, SwiGLU) has no CPU arm; the dit, ffn, attention and "
-                          "quant workloads have one"}), flush=True)
         return
     vals = [cpu_baseline_run(args) for _ in range(max(args.steps, 1))]
     v = statistics.median([r["value"] for r in vals])
@@ -624,9 +657,11 @@ def run_reference(args) -> None:
                "ffn": lambda: FFNWorkload.describe(args.gpus),
                "quant": lambda: QuantWorkload.describe(args.gpus),
                "attention": lambda: AttentionWorkload.describe(
-                   args.gpus, [int(n) for n in args.attn_docs.split(",")])}
+                   args.gpus, [int(n) for n in args.attn_docs.split(",")]),
+               "refblock": lambda: RefBlockWorkload.describe(args.gpus)}
     dtypes = {"dit": "fp32 (NVFP4 operands decoded)", "ffn": "fp32 (NVFP4 operands decoded)",
-              "quant": "fp32 -> e2m1 / e4m3", "attention": "fp32 (bf16 q|k|v)"}
+              "quant": "fp32 -> e2m1 / e4m3", "attention": "fp32 (bf16 q|k|v)",
+              "refblock": "fp32 (NVFP4 operands decoded)"}
     line = {
         "impl": "reference", "metric": METRIC, "value": v, "unit": unit,
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,

@@ -60,22 +60,33 @@ def rmsnorm(x: torch.Tensor, gamma: torch.Tensor, eps: float) -> torch.Tensor:
 
 
 class FFNBlockCPU:
-    """RMSNorm -> NVFP4 linear(+b1) -> GELU-tanh -> re-quant -> NVFP4 linear(+b2) + x."""
+    """RMSNorm -> NVFP4 linear(+b1) -> GELU-tanh -> re-quant -> NVFP4 linear(+b2) + x;
+    ``act="swiglu"``: w1 is the fused [value | gate] projection (2F rows, no
+    biases) and the activation is bf16(value * bf16(silu(gate))), the
+    reference's SwiGLU (h3_inference/transformer/ops.py:62-71)."""
 
-    def __init__(self, w1, b1, w2, b2, gamma, eps):
+    def __init__(self, w1, b1, w2, b2, gamma, eps, act: str = "gelu_tanh"):
+        if act not in ("gelu_tanh", "swiglu"):
+            raise ValueError(act)
         c1, s1, g1 = quantize(w1.to(torch.bfloat16).float())
         c2, s2, g2 = quantize(w2.to(torch.bfloat16).float())
         self.w1 = dequantize(c1, s1, g1)          # fp32, decoded once like a loaded checkpoint
         self.w2 = dequantize(c2, s2, g2)
-        self.b1 = b1.to(torch.bfloat16).float()
-        self.b2 = b2.to(torch.bfloat16).float()
+        self.b1 = None if b1 is None else b1.to(torch.bfloat16).float()
+        self.b2 = None if b2 is None else b2.to(torch.bfloat16).float()
         self.gamma = gamma.to(torch.bfloat16)
         self.eps = eps
+        self.act = act
 
     def __call__(self, x: torch.Tensor, gs_h: float | None = None, gs_u: float | None = None):
         h = rmsnorm(x, self.gamma, self.eps)
         ch, sh, gh = quantize(h.float(), gs_h)
-        u = F.gelu(F.linear(dequantize(ch, sh, gh), self.w1, self.b1), approximate="tanh")
+        u = F.linear(dequantize(ch, sh, gh), self.w1, self.b1)
+        if self.act == "swiglu":
+            val, gate = u.to(torch.bfloat16).float().chunk(2, dim=-1)
+            u = val * F.silu(gate).to(torch.bfloat16).float()
+        else:
+            u = F.gelu(u, approximate="tanh")
         u = u.to(torch.bfloat16)
         cu, su, gu = quantize(u.float(), gs_u)
         y = F.linear(dequantize(cu, su, gu), self.w2, self.b2) + x.float()

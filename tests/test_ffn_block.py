@@ -60,6 +60,22 @@ def test_cpu_port_ffn_matches_oracle():
     assert R.max_rel_err(y, ref) <= TOL
 
 
+def test_cpu_port_swiglu_ffn_matches_oracle():
+    """The timed CPU port of the reference-shape FFN half (SwiGLU) against the
+    oracle's restatement (no modulation, gate or bias)."""
+    g = torch.Generator().manual_seed(12)
+    T, d, f = 48, 256, 256
+    x = torch.randn(T, d, generator=g).to(torch.bfloat16)
+    wu = (torch.randn(2 * f, d, generator=g) * 0.05).to(torch.bfloat16)
+    wd = (torch.randn(d, f, generator=g) * 0.05).to(torch.bfloat16)
+    gamma = (1 + 0.1 * torch.randn(d, generator=g)).to(torch.bfloat16)
+    blk = C.FFNBlockCPU(wu, None, wd, None, gamma, 1e-5, act="swiglu")
+    y = blk(x).float().numpy()
+    ref, _ = B.swiglu_ffn_block_mod(x.float().numpy(), gamma.float().numpy(), 1e-5,
+                                    oracle_weights(wu), oracle_weights(wd))
+    assert R.max_rel_err(y, ref) <= TOL
+
+
 @pytest.mark.gpu
 @pytest.mark.parametrize("T,d,f", [(256, 512, 2048), (200, 768, 1536)])
 def test_ffn_block_matches_oracle(cuda, T, d, f):
