@@ -62,11 +62,13 @@ METRIC = "NVFP4 GEMM TFLOP/s/GPU & % FP4 peak; DiT block latency at 1/2/4/8 B200
 FFN_TOKENS, HIDDEN, FFN = 32768, 3072, 12288
 # Per-launch DRAM traffic (dram__bytes_read.sum + dram__bytes_write.sum) of
 # the kernel named in the roofline object, from one ncu capture each:
-#   k_fmha: 183.2 MB at 8192 tokens (q|k|v read once, O written), linear in
-#     tokens -> 2 x 33784 tokens of the DiT attention launch = 1.511 GB; for
-#     the attention workload the same per-token figure times its tokens.
+#   k_fmha: 639.9 MB read + 187.8 MB written = 827.6 MB for one launch on the
+#     32760 + 1024-token packing (24 heads; q|k|v 622.7 MB read once, O
+#     207.6 MB of which 187.8 MB reached DRAM inside the launch), i.e. per
+#     token of the launch; the DiT launch (the CFG pair stacked, 2 x 33784
+#     tokens) is the same per-token figure times its tokens.
 #   k_gemm_nvfp4: FFN up 835.5 MB, down 639.4 MB at 32768 tokens (mean).
-ATTN_TRAFFIC_PER_TOKEN = (151.128064e6 + 32.116736e6) / 8192
+ATTN_TRAFFIC_PER_TOKEN = (639878656 + 187751424) / 33784
 TRAFFIC_BYTES: dict[str, float | None] = {"k_fmha": ATTN_TRAFFIC_PER_TOKEN * 2 * 33784,
                                           "k_gemm_nvfp4": (835.5e6 + 639.4e6) / 2}
 
@@ -164,11 +166,17 @@ class DiTWorkload:
         self.rank_attn_flops = self.cfg.blocks * branches * sum(
             4 * hd * max(0, min(b, r1) - max(a, r0)) * (b - a) for a, b in doc_of)
         self.attn_launches_per_step = self.cfg.blocks
-        # DRAM bytes of one attention launch on this rank: q rows read once
-        # (6144 B) and their output written (3920 B measured of 6144), every
-        # K|V row of the local branches read once (12288 B)
+        # DRAM bytes of one attention launch on this rank, from the full-size
+        # capture (ATTN_TRAFFIC_PER_TOKEN): per query row its q read (6144 B)
+        # and 5557 B of its output written inside the launch; per key row
+        # 12797 B read (K|V once, +4 % re-reads)
         q_rows, kv_rows = rows * branches, T * branches
-        self.attn_traffic = q_rows * (6144 + 3920.5) + kv_rows * 12288
+        self.attn_traffic = q_rows * (6144 + 187751424 / 33784) + kv_rows * (
+            (639878656 - 6144 * 33784) / 33784)
+        # the block GEMM shapes of the stacked CFG pair (rows padded to 128 by the GEMM)
+        M2 = 2 * T
+        self.library_shapes = {"qkv": (M2, 3 * hd, d), "out": (M2, d, hd), "up": (M2, ff, d),
+                               "down": (M2, d, ff), "square_8192": (8192, 8192, 8192)}
         self.config = self.describe(world)
 
     @staticmethod
@@ -756,7 +764,13 @@ def run_ours(args) -> None:
     if world == 1 and wl.name == "dit" and not args.no_extras:
         extras["cuda_graph"] = graph_step_timing(wl, args.steps)
     if rank == 0 and not args.no_extras:
-        extras["library_gemm_torch_scaled_mm"] = library_gemm_reference(dev)
+        extras["library_gemm_torch_scaled_mm"] = library_gemm_reference(
+            dev, getattr(wl, "library_shapes", None))
+        if wl.name in ("attention", "dit"):
+            docs = ([b - a for a, b in zip(wl.cu[:-1], wl.cu[1:])] if wl.name == "attention"
+                    else [b - a for a, b in zip(wl.cfg.cu_seqlens()[:-1], wl.cfg.cu_seqlens()[1:])])
+            extras["library_attention_sdpa"] = library_attention_sdpa(
+                dev, docs, copies=1 if wl.name == "attention" else 2)
         cpu = cpu_baseline_run(args) if world == 1 else None
         if cpu is not None:
             extras["cpu_baseline"] = {k: cpu[k] for k in ("value", "unit", "cores", "kind", "sample")}
@@ -783,11 +797,11 @@ def run_ours(args) -> None:
             n_launch = len(gemm_ev)
             flops_launch = wl.rank_gemm_flops * args.steps / max(n_launch, 1)
             achieved = wl.rank_gemm_flops / (gemm_ms * 1e-3) / 1e12
-            peak = 4.0 * pk["bf16_sustained"]
+            peak, source = fp4_peak(extras.get("library_gemm_torch_scaled_mm"), pk)
             roof = {"bound": "tensor", "kernel": "h3b::gemm::k_gemm_nvfp4", "achieved": achieved,
                     "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
-                    "peak_source": f"4 x bf16_tflops_sustained of {pk['source']} "
-                                   "MEASURED_PEAKS.json (dense FP4 = 4x bf16 on B200)",
+                    "peak_source": source,
+                    "frac_of_nominal_9pf": achieved / NOMINAL_FP4_TFLOPS,
                     "traffic": TRAFFIC_BYTES["k_gemm_nvfp4"],
                     "per_launch_tflop": flops_launch / 1e12, "share_of_step": gemm_ms / ms}
         if hasattr(wl, "step_bytes"):           # memory-bound workload: GB/s
@@ -811,8 +825,11 @@ def run_ours(args) -> None:
                     "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
             "roofline": roof,
             "nvfp4_gemm_tflops_per_gpu": gemm_tflops,
-            "nvfp4_gemm_frac_of_fp4_peak": (gemm_tflops / (4.0 * pk["bf16_sustained"])
-                                            if gemm_tflops else None),
+            "nvfp4_gemm_frac_of_fp4_peak": (gemm_tflops / fp4_peak(
+                extras.get("library_gemm_torch_scaled_mm"), pk)[0] if gemm_tflops else None),
+            "fp4_peak_source": fp4_peak(extras.get("library_gemm_torch_scaled_mm"), pk)[1],
+            "nvfp4_gemm_frac_of_nominal_9pf": (gemm_tflops / NOMINAL_FP4_TFLOPS
+                                               if gemm_tflops else None),
             "gpu_launches": int(launches),
             "clocks": clk.summary(),
         }
@@ -844,33 +861,101 @@ def graph_step_timing(wl, steps: int) -> dict:
     return {"ms_per_step": ms, "value": wl.step_flops / (ms * 1e-3) / 1e12, "unit": "TFLOP/s"}
 
 
-def library_gemm_reference(dev) -> dict | None:
-    """torch._scaled_mm (cuBLASLt NVFP4, the reference's GEMM call) on the FFN
-    GEMM shapes, for context; not part of the timed step."""
+def library_gemm_reference(dev, shapes: dict | None = None) -> dict | None:
+    """torch._scaled_mm (cuBLASLt NVFP4, the reference's GEMM call at
+    h3_inference/nvfp4.py:112-115) on 8192^3 and the GEMM shapes of the
+    workloads, best of 3 runs of 10 back-to-back launches each: the measured
+    dense-FP4 rate the GEMM fractions are quoted against.  Not part of the
+    timed step."""
     try:
         from h3_engine_b200 import ops
         out = {}
-        for name, (M, N, K) in {"up": (FFN_TOKENS, FFN, HIDDEN),
-                                "down": (FFN_TOKENS, HIDDEN, FFN)}.items():
+        shapes = shapes or {"up": (FFN_TOKENS, FFN, HIDDEN), "down": (FFN_TOKENS, HIDDEN, FFN),
+                            "square_8192": (8192, 8192, 8192)}
+        for name, (M, N, K) in shapes.items():
             a = torch.randn(M, K, device=dev).to(torch.bfloat16)
             b = (torch.randn(N, K, device=dev) * 0.02).to(torch.bfloat16)
-            qa, sa, _ = ops.quantize(a, mpad=M, gs=1.0)
+            qa, sa, _ = ops.quantize(a, mpad=ops.pad_m(M), gs=1.0)
             qb, sb, _ = ops.quantize(b, mpad=N, gs=1.0)
             a4, b4 = qa.view(torch.float4_e2m1fn_x2), qb.view(torch.float4_e2m1fn_x2).t()
             s1, s2 = sa.view(torch.float8_e4m3fn), sb.view(torch.float8_e4m3fn)
             for _ in range(3):
                 torch._scaled_mm(a4, b4, s1, s2, out_dtype=torch.bfloat16)
-            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            e0.record()
-            for _ in range(10):
-                torch._scaled_mm(a4, b4, s1, s2, out_dtype=torch.bfloat16)
-            e1.record()
-            torch.cuda.synchronize()
-            ms = e0.elapsed_time(e1) / 10
-            out[name] = {"ms": ms, "tflops": 2.0 * M * N * K / (ms * 1e-3) / 1e12}
+            best = None
+            for _ in range(3):
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record()
+                for _ in range(10):
+                    torch._scaled_mm(a4, b4, s1, s2, out_dtype=torch.bfloat16)
+                e1.record()
+                torch.cuda.synchronize()
+                ms = e0.elapsed_time(e1) / 10
+                best = ms if best is None else min(best, ms)
+            mp = qa.shape[0]
+            out[name] = {"shape": [M, N, K], "ms": best,
+                         "tflops": 2.0 * mp * N * K / (best * 1e-3) / 1e12}
             del a, b, qa, qb
         return out
     except Exception as ex:  # pragma: no cover - library availability varies
+        return {"unavailable": str(ex)[:160]}
+
+
+def fp4_peak(lib: dict | None, pk: dict) -> tuple[float, str]:
+    """Denominator of the NVFP4 GEMM fractions: the best cuBLASLt NVFP4 rate
+    measured in this run (a dense-FP4 rate the library reaches on this GPU at
+    this clock), else 4 x the measured bf16 burst rate."""
+    rates = [v["tflops"] for v in (lib or {}).values() if isinstance(v, dict) and "tflops" in v]
+    if rates:
+        return max(rates), ("best torch._scaled_mm NVFP4 (cuBLASLt) rate measured in this run "
+                            "over 8192^3 and the workload's GEMM shapes")
+    return 4.0 * pk["bf16"], (f"4 x bf16_tflops (burst) of {pk['source']} MEASURED_PEAKS.json "
+                              "(no library FP4 measurement in this run)")
+
+
+NOMINAL_FP4_TFLOPS = 9000.0     # B200 dense FP4 (the 9 PFLOP/s figure the targets quote)
+
+
+def library_attention_sdpa(dev, docs: list[int], heads: int = 24, head_dim: int = 128,
+                           copies: int = 1) -> dict | None:
+    """F.scaled_dot_product_attention (the reference's attention call,
+    h3_inference/kernels/packed_self_attn.py:34-36) on the same packing, one
+    call per document ([1, H, L, D] bf16, non-causal), with the cuDNN and the
+    flash backends, best of 3 runs of 5; ``copies`` repeats the documents
+    (the CFG pair)."""
+    try:
+        import torch.nn.functional as F
+        from torch.nn.attention import SDPBackend, sdpa_kernel
+        g = torch.Generator(device=dev).manual_seed(77)
+        tensors = [[torch.randn(1, heads, n, head_dim, generator=g, device=dev).to(torch.bfloat16)
+                    for _ in range(3)] for n in docs]
+        flops = copies * sum(4 * heads * head_dim * n * n for n in docs)
+        out = {}
+        for name, be in (("cudnn", SDPBackend.CUDNN_ATTENTION), ("flash", SDPBackend.FLASH_ATTENTION)):
+            try:
+                with sdpa_kernel([be]):
+                    def run():
+                        for _ in range(copies):
+                            for q, k, v in tensors:
+                                F.scaled_dot_product_attention(q, k, v)
+                    run()
+                    torch.cuda.synchronize()
+                    best = None
+                    for _ in range(3):
+                        e0 = torch.cuda.Event(enable_timing=True)
+                        e1 = torch.cuda.Event(enable_timing=True)
+                        e0.record()
+                        for _ in range(5):
+                            run()
+                        e1.record()
+                        torch.cuda.synchronize()
+                        ms = e0.elapsed_time(e1) / 5
+                        best = ms if best is None else min(best, ms)
+                out[name] = {"ms": best, "tflops": flops / (best * 1e-3) / 1e12}
+            except Exception as ex:   # backend not available for this shape / build
+                out[name] = {"unavailable": str(ex)[:120]}
+        del tensors
+        return out
+    except Exception as ex:  # pragma: no cover
         return {"unavailable": str(ex)[:160]}
 
 

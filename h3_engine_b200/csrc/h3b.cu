@@ -531,21 +531,50 @@ static __device__ __align__(256) float g_noalloc_scratch[kNoAllocRows + 64];
 namespace h3b {
 constexpr int kNoAllocMaxDevices = 64;
 static float* g_noalloc_ptr[kNoAllocMaxDevices];
+static CUcontext g_noalloc_ctx[kNoAllocMaxDevices];
 static std::mutex g_noalloc_mu;
+
+// The driver's current context, through the runtime's driver entry point
+// (the library links only cudart).
+static int current_context(CUcontext* ctx) {
+  using Fn = CUresult (*)(CUcontext*);
+  static Fn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<Fn>(p);
+  });
+  if (!fn || fn(ctx) != CUDA_SUCCESS) return H3B_ERR_CUDA;
+  return H3B_OK;
+}
 
 // Device address of g_noalloc_scratch on the current device.  In host code the
 // symbol itself is only a host-side stand-in, so the address is looked up with
-// cudaGetSymbolAddress once per device (with that device current) and cached.
+// cudaGetSymbolAddress (with the device current) and cached per device,
+// together with the context it belongs to: after a device reset the runtime
+// creates a new context and loads the module again, so a context change
+// triggers a fresh lookup instead of reusing a stale address.
 static int noalloc_scratch(float** out) {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return H3B_ERR_CUDA;
   if (dev < 0 || dev >= kNoAllocMaxDevices) return H3B_ERR_UNSUPPORTED;
+  // NULL before the runtime has made this device's primary context current
+  CUcontext ctx = nullptr;
+  int rc = current_context(&ctx);
+  if (rc != H3B_OK) return rc;
   std::lock_guard<std::mutex> lock(g_noalloc_mu);
-  if (g_noalloc_ptr[dev] == nullptr) {
+  if (g_noalloc_ptr[dev] == nullptr || ctx == nullptr || g_noalloc_ctx[dev] != ctx) {
     void* p = nullptr;
+    // the lookup itself initialises the primary context when needed
     if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess || p == nullptr)
       return H3B_ERR_CUDA;
+    rc = current_context(&ctx);
+    if (rc != H3B_OK) return rc;
     g_noalloc_ptr[dev] = static_cast<float*>(p);
+    g_noalloc_ctx[dev] = ctx;
   }
   *out = g_noalloc_ptr[dev];
   return H3B_OK;

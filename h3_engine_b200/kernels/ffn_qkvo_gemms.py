@@ -12,9 +12,10 @@ Same functions, signatures and env flags as the reference:
                             stock expression, eagerly
 * ``context_projection`` -- the linear itself (:56-58)
 
-"Quantized" means the linears were replaced by this library's
-``nvfp4._QuantLinear`` (``quantize_blocks`` / ``load_quantized``); other
-linears take the reference's stock path.
+"Quantized" means the linears carry an NVFP4 weight: this library's
+``nvfp4._QuantLinear`` (``quantize_blocks`` / ``load_quantized``) or the
+reference's own quantized linear (same packed format, read with global
+scale 1); other linears take the reference's stock path.
 """
 from __future__ import annotations
 
@@ -34,16 +35,20 @@ def qkv_kernel(to_q, to_k, to_v, x: torch.Tensor):
 
 def out_kernel(to_out, x: torch.Tensor):
     from h3_engine_b200 import nvfp4
-    if not (x.is_cuda and isinstance(to_out, nvfp4._QuantLinear)):
+    if not (x.is_cuda and nvfp4._is_quant_linear(to_out)):
         return MISS
-    return to_out(x)
+    if isinstance(to_out, nvfp4._QuantLinear):
+        return to_out(x)
+    # the reference's own quantized linear: same weight format, global scale 1
+    to_out.calls = getattr(to_out, "calls", 0) + 1
+    return nvfp4.QuantizedActivation(x).mm(to_out.weight_nvfp4)
 
 
 def _swiglu_weight(lin):
     """The up-projection's packed weight with its rows in the order the
     SwiGLU epilogue reads (``ops.swiglu_rows``), cached on the module."""
     from h3_engine_b200 import nvfp4, ops
-    w = lin.weight_nvfp4
+    w = nvfp4.as_nvfp4_weight(lin.weight_nvfp4)
     cached = getattr(lin, "_h3b_swiglu", None)
     if cached is not None and cached[0] is w:
         return cached[1]
@@ -65,7 +70,7 @@ def ffn_kernel(ff: nn.Module, x: torch.Tensor):
     gate_mod, down = net[0], net[2]
     up = getattr(gate_mod, "proj", None)
     act_fn = getattr(gate_mod, "activation", None)
-    if not (isinstance(up, nvfp4._QuantLinear) and isinstance(down, nvfp4._QuantLinear)):
+    if not (nvfp4._is_quant_linear(up) and nvfp4._is_quant_linear(down)):
         return MISS
     if act_fn is not None and not isinstance(act_fn, nn.SiLU):
         return MISS
@@ -82,11 +87,11 @@ def ffn_kernel(ff: nn.Module, x: torch.Tensor):
                  a.rows, wq, wsf, wgs, 2 * f, up.in_features, act=ops.ACT_SWIGLU,
                  amax_out=amax)
     qh, sfh, gsh = ops.quantize(h, mpad=ops.pad_m(a.rows), amax_t=amax)
-    wd = down.weight_nvfp4
+    wd = nvfp4.as_nvfp4_weight(down.weight_nvfp4)
     y = ops.gemm(qh, sfh, gsh, a.rows, wd.qdata, wd.scale_u8, wd.global_scale,
                  down.out_features, f)
-    up.calls += 1
-    down.calls += 1
+    up.calls = getattr(up, "calls", 0) + 1
+    down.calls = getattr(down, "calls", 0) + 1
     return y.reshape(*x.shape[:-1], down.out_features)
 
 

@@ -75,37 +75,38 @@ def _quantize(x: torch.Tensor, global_scale: float | None = None):
 
 
 class _PadCache:
-    """Per-(rows, cols) padded buffers, allocated once and reused
-    (h3_inference/nvfp4.py:61-87)."""
+    """Row-padded NVFP4 buffers reused across calls, one per (kind, rows,
+    columns, device, dtype).  ``data`` / ``scale`` are the accessors of the
+    reference's cache (h3_inference/nvfp4.py:61-87).  The buffers are left
+    uninitialised: the quantizer writes every row up to the padded count,
+    padding rows as zero codes and zero scales."""
+
+    __slots__ = ("_store",)
 
     def __init__(self) -> None:
-        self._data: dict[tuple, torch.Tensor] = {}
-        self._scale: dict[tuple, torch.Tensor] = {}
+        self._store: dict[tuple, torch.Tensor] = {}
+
+    def _get(self, kind: str, rows: int, cols: int, device, dtype) -> torch.Tensor:
+        key = (kind, int(rows), int(cols), torch.device(device), dtype)
+        buf = self._store.get(key)
+        if buf is None:
+            buf = self._store[key] = torch.empty((rows, cols), device=device, dtype=dtype)
+        return buf
 
     def data(self, rows: int, cols: int, device, dtype) -> torch.Tensor:
-        key = (rows, cols, device, dtype)
-        buf = self._data.get(key)
-        if buf is None:
-            buf = torch.zeros(rows, cols, device=device, dtype=dtype)
-            self._data[key] = buf
-        return buf
+        return self._get("codes", rows, cols, device, dtype)
 
     def scale(self, rows: int, cols: int, device, dtype) -> torch.Tensor:
-        key = (rows, cols, device, dtype)
-        buf = self._scale.get(key)
-        if buf is None:
-            buf = torch.zeros(rows, cols, device=device, dtype=dtype)
-            self._scale[key] = buf
-        return buf
+        return self._get("scales", rows, cols, device, dtype)
 
     def clear(self) -> None:
-        self._data.clear()
-        self._scale.clear()
+        self._store.clear()
 
 
+# _quantize_padded's buffers (row-major scales, as the reference returns them)
 _PAD = _PadCache()
-# QuantizedActivation writes swizzled scales straight into its own buffers
-# (the reference swizzles a copy of _PAD's row-major scales instead).
+# QuantizedActivation's buffers: the quantizer writes the swizzled scales the
+# GEMM reads straight into them, so no separate swizzle pass runs
 _ACT = _PadCache()
 
 
@@ -224,7 +225,10 @@ class QuantizedActivation:
         self.scale_blocked = sf.view(-1).view(torch.float8_e4m3fn)
         self.global_scale = gs
 
-    def mm(self, w: NVFP4Weight, out: torch.Tensor | None = None) -> torch.Tensor:
+    def mm(self, w, out: torch.Tensor | None = None) -> torch.Tensor:
+        """``x @ w.T`` for this library's ``NVFP4Weight`` or a weight object of
+        the reference's own ``nvfp4`` module (read with global scale 1)."""
+        w = as_nvfp4_weight(w)
         k = self.shape[-1]
         if w.in_features != k:
             raise ValueError(f"in_features {w.in_features} != activation K {k}")
@@ -234,151 +238,210 @@ class QuantizedActivation:
         return y.reshape(*self.shape[:-1], w.out_features)
 
 
-def nvfp4_linear(w: NVFP4Weight, x: torch.Tensor) -> torch.Tensor:
+def as_nvfp4_weight(w) -> NVFP4Weight:
+    """This library's ``NVFP4Weight`` for ``w``.  A weight built by the
+    reference's own ``nvfp4`` module (slots ``qdata_t`` -- the packed codes
+    viewed transposed -- and ``scale`` -- the swizzled e4m3 scales --, no
+    global scale, h3_inference/nvfp4.py:48-59) is wrapped without copying,
+    with the two-level scheme's global scale 1; the wrapper is cached on the
+    object when it allows attributes, else rebuilt per call (a view)."""
+    if isinstance(w, NVFP4Weight):
+        return w
+    cached = getattr(w, "_h3b_weight", None)
+    if cached is not None and cached.qdata_t.data_ptr() == w.qdata_t.data_ptr():
+        return cached
+    n, k = int(w.out_features), int(w.in_features)
+    packed = w.qdata_t.t().view(torch.uint8)
+    gs = getattr(w, "global_scale", None)
+    mine = NVFP4Weight.from_packed(packed, w.scale, n, k, gs, getattr(w, "dtype", torch.bfloat16))
+    try:
+        object.__setattr__(w, "_h3b_weight", mine)
+    except (AttributeError, TypeError):
+        pass
+    return mine
+
+
+def nvfp4_linear(w, x: torch.Tensor) -> torch.Tensor:
     """``x @ w.T`` in NVFP4 (h3_inference/nvfp4.py:118-120)."""
     return QuantizedActivation(x).mm(w)
 
 
-def _block_linears(block: nn.Module) -> Iterable[tuple[nn.Module, str, nn.Linear]]:
-    """h3_inference/nvfp4.py:122-130."""
-    attn = block.attn
-    yield attn, "to_q", attn.to_q
-    yield attn, "to_k", attn.to_k
-    yield attn, "to_v", attn.to_v
-    yield attn.to_out, "0", attn.to_out[0]
-    ff = block.ff
-    yield ff.net[0], "proj", ff.net[0].proj
-    yield ff.net, "2", ff.net[2]
+# The six linears of a transformer block that the NVFP4 path replaces, as
+# (parent module path inside the block, child name): q, k, v, the output
+# projection, the fused SwiGLU [value | gate] projection and the down
+# projection -- the set and order of h3_inference/nvfp4.py:122-130.
+_BLOCK_LINEAR_SLOTS = (("attn", "to_q"), ("attn", "to_k"), ("attn", "to_v"),
+                       ("attn.to_out", "0"), ("ff.net.0", "proj"), ("ff.net", "2"))
+
+
+def _block_linears(block: nn.Module) -> Iterable[tuple[nn.Module, str, nn.Module]]:
+    """(parent, child name, module) of each replaced linear of ``block``."""
+    for path, name in _BLOCK_LINEAR_SLOTS:
+        parent = block.get_submodule(path)
+        yield parent, name, parent._modules[name]
+
+
+def _suffix_for(parent, attr: str, block) -> str:
+    """Checkpoint key suffix (``attn.to_q.weight``, ``ff.net.0.proj.weight``,
+    ...) of the linear ``parent.<attr>`` of ``block`` (the key format of
+    h3_inference/nvfp4.py:284-293)."""
+    for path, name in _BLOCK_LINEAR_SLOTS:
+        if name == attr and block.get_submodule(path) is parent:
+            return f"{path}.{name}.weight"
+    raise KeyError(f"unmapped block Linear: {parent}.{attr}")
+
+
+def _set_child(parent: nn.Module, name: str, module: nn.Module) -> None:
+    """Replace a registered child (a named attribute or a numbered slot of a
+    ModuleList / Sequential alike: both live in ``_modules``)."""
+    parent._modules[name] = module
 
 
 class _QuantLinear(nn.Module):
-    """h3_inference/nvfp4.py:132-144 (raises on a bias like the reference)."""
+    """An NVFP4 linear without bias (the reference's module,
+    h3_inference/nvfp4.py:132-144: attributes ``weight_nvfp4``,
+    ``in_features``, ``out_features`` and the ``calls`` counter; a linear
+    with a bias is refused with the reference's error)."""
 
     def __init__(self, linear: nn.Linear):
         super().__init__()
         if linear.bias is not None:
             raise NotImplementedError("NVFP4 path does not carry a bias term")
-        self.weight_nvfp4 = NVFP4Weight(linear.weight.data)
-        self.in_features = linear.in_features
-        self.out_features = linear.out_features
+        self._bind(NVFP4Weight(linear.weight.data))
+
+    def _bind(self, weight: NVFP4Weight) -> None:
+        self.weight_nvfp4 = weight
+        self.in_features, self.out_features = weight.in_features, weight.out_features
         self.calls = 0
+
+    @classmethod
+    def from_weight(cls, weight: NVFP4Weight) -> "_QuantLinear":
+        """Wrap an already-quantized weight (checkpoint loading)."""
+        mod = cls.__new__(cls)
+        nn.Module.__init__(mod)
+        mod._bind(weight)
+        return mod
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         self.calls += 1
-        return nvfp4_linear(self.weight_nvfp4, x)
+        return QuantizedActivation(x).mm(self.weight_nvfp4)
+
+
+def _is_quant_linear(m) -> bool:
+    """True for this library's ``_QuantLinear`` and for any module carrying
+    an NVFP4 weight object in ``weight_nvfp4`` (the reference's own
+    ``_QuantLinear``)."""
+    w = getattr(m, "weight_nvfp4", None)
+    return w is not None and hasattr(w, "qdata_t") and hasattr(w, "scale")
+
+
+_GIB = float(1 << 30)
 
 
 @torch.no_grad()
 def quantize_blocks(model, self_check: bool = True) -> dict:
-    """h3_inference/nvfp4.py:146-167."""
+    """Swap the six block linears of every transformer block for NVFP4
+    ones, after the optional self-check (h3_inference/nvfp4.py:146-167; same
+    return keys).  Only (parent, name) pairs are collected up front, so each
+    bf16 weight is released as soon as its replacement is in place and
+    ``freed_gib`` sees it."""
     if self_check and os.environ.get("H3_NVFP4_SELFCHECK") != "0":
         run_self_check(model)
-    before = torch.cuda.memory_allocated()
-    replaced = 0
-    for block in model.transformer_blocks:
-        for parent, attr, linear in list(_block_linears(block)):
-            q = _QuantLinear(linear)
-            if isinstance(parent, (nn.ModuleList, nn.Sequential)):
-                parent[int(attr)] = q
-            else:
-                setattr(parent, attr, q)
-            replaced += 1
+    mem0 = torch.cuda.memory_allocated()
+    slots = [(parent, name) for block in model.transformer_blocks
+             for parent, name, _ in _block_linears(block)]
+    for parent, name in slots:
+        _set_child(parent, name, _QuantLinear(parent._modules[name]))
     torch.cuda.empty_cache()
-    after = torch.cuda.memory_allocated()
-    return {
-        "linears_quantized": replaced,
-        "freed_gib": (before - after) / 1024**3,
-        "resident_gib": after / 1024**3,
-    }
+    mem1 = torch.cuda.memory_allocated()
+    return {"linears_quantized": len(slots), "freed_gib": (mem0 - mem1) / _GIB,
+            "resident_gib": mem1 / _GIB}
 
 
 @torch.no_grad()
 def run_self_check(model, tol: float = 0.98) -> float:
-    """cos >= 0.98 against bf16 F.linear (h3_inference/nvfp4.py:169-181)."""
-    linear = model.transformer_blocks[0].attn.to_q
-    w = linear.weight.data
-    x = torch.randn(M_ALIGN * 2, w.shape[1], device=w.device, dtype=torch.bfloat16)
-    ref = torch.nn.functional.linear(x, w.to(torch.bfloat16))
-    got = nvfp4_linear(NVFP4Weight(w), x)
-    cos = float(torch.nn.functional.cosine_similarity(ref.float().flatten(),
-                                                      got.float().flatten(), dim=0))
+    """Cosine similarity of the NVFP4 linear against the bf16 one on random
+    rows, for the first block's query projection; raises below ``tol`` (the
+    reference's check and message, h3_inference/nvfp4.py:169-181).  The row
+    count is not a multiple of 128, so the padded-row path is exercised."""
+    w = model.transformer_blocks[0].attn.to_q.weight.data
+    gen = torch.Generator(device=w.device).manual_seed(0)
+    x = torch.randn(3 * M_ALIGN - 37, w.shape[1], generator=gen, device=w.device)
+    x = x.to(torch.bfloat16)
+    ref = torch.nn.functional.linear(x, w.to(torch.bfloat16)).float().flatten()
+    got = nvfp4_linear(NVFP4Weight(w), x).float().flatten()
+    cos = float(torch.dot(ref, got) / (ref.norm() * got.norm()).clamp_min(1e-30))
     if cos < tol:
         raise RuntimeError(f"NVFP4 self-check failed: cos {cos:.5f} < {tol}. ")
     return cos
 
 
-def _suffix_for(parent, attr: str, block) -> str:
-    """h3_inference/nvfp4.py:284-293."""
-    if parent is block.attn:
-        return f"attn.{attr}.weight"
-    if parent is block.attn.to_out:
-        return f"attn.to_out.{attr}.weight"
-    if parent is block.ff.net[0]:
-        return f"ff.net.0.{attr}.weight"
-    if parent is block.ff.net:
-        return f"ff.net.{attr}.weight"
-    raise KeyError(f"unmapped block Linear: {parent}.{attr}")
+_PACKED_SUFFIXES = ("_nvfp4", "_nvfp4_scale", "_nvfp4_global_scale")
+
+
+def _checkpoint_index(folder) -> dict[str, str]:
+    """tensor name -> shard file, from the folder's safetensors index."""
+    import json
+    index = next(iter(sorted(folder.glob("*.safetensors.index.json"))), None)
+    if index is None:
+        raise FileNotFoundError(f"no safetensors index under {folder}")
+    return json.loads(index.read_text())["weight_map"]
 
 
 @torch.no_grad()
 def load_quantized(model, path: str) -> dict:
-    """Swap each block linear for one rebuilt from ``<key>_nvfp4`` /
-    ``<key>_nvfp4_scale`` (+ optional ``<key>_nvfp4_global_scale``, absent ->
-    1.0) tensors (h3_inference/nvfp4.py:231-282)."""
-    import json
+    """Replace every block linear by an NVFP4 one rebuilt from the packed
+    checkpoint tensors ``<key>_nvfp4`` (u8 [N, K/2]) and ``<key>_nvfp4_scale``
+    (swizzled e4m3), plus the optional ``<key>_nvfp4_global_scale`` (absent:
+    1.0, the two-level scheme).  Same keys, errors and return value as
+    h3_inference/nvfp4.py:231-282.  Every linear is matched to its keys before
+    any is replaced, then each shard is opened once for exactly the tensors
+    it holds."""
     from pathlib import Path
 
     from safetensors import safe_open
 
     folder = Path(path)
-    index = next(folder.glob("*.safetensors.index.json"), None)
-    if index is None:
-        raise FileNotFoundError(f"no safetensors index under {folder}")
-    weight_map = json.loads(index.read_text())["weight_map"]
-    wanted: dict[str, tuple[str, str]] = {}
-    for key in weight_map:
-        if key.endswith("_nvfp4"):
-            wanted[key[: -len("_nvfp4")]] = (key, key + "_scale")
-    if not wanted:
+    weight_map = _checkpoint_index(folder)
+    packed = {k[: -len("_nvfp4")] for k in weight_map if k.endswith("_nvfp4")}
+    if not packed:
         raise RuntimeError(f"{folder} carries no `_nvfp4` weights — is it the bf16 checkpoint?")
-
+    plan = []
+    for i, block in enumerate(model.transformer_blocks):
+        for parent, name, lin in _block_linears(block):
+            key = f"transformer_blocks.{i}." + _suffix_for(parent, name, block)
+            if key not in packed:
+                raise KeyError(f"pre-quantized checkpoint is missing {key}_nvfp4")
+            plan.append((parent, name, key, lin.in_features, lin.out_features))
+    by_shard: dict[str, list[str]] = {}
+    for *_, key, _, _ in plan:
+        for suffix in _PACKED_SUFFIXES:
+            shard = weight_map.get(key + suffix)
+            if shard is not None:
+                by_shard.setdefault(shard, []).append(key + suffix)
     device = next((p.device for p in model.parameters() if not p.is_meta), torch.device("cuda"))
     tensors: dict[str, torch.Tensor] = {}
-    shards = {weight_map[k] for pair in wanted.values() for k in pair}
-    shards |= {weight_map[k] for k in weight_map if k.endswith("_nvfp4_global_scale")}
-    for shard in sorted(shards):
+    for shard, names in sorted(by_shard.items()):
         with safe_open(str(folder / shard), framework="pt", device=str(device)) as f:
-            for name in f.keys():
-                if name.endswith(("_nvfp4", "_nvfp4_scale", "_nvfp4_global_scale")):
-                    tensors[name] = f.get_tensor(name)
-
-    replaced = 0
-    for block_index, block in enumerate(model.transformer_blocks):
-        for parent, attr, linear in list(_block_linears(block)):
-            prefix = f"transformer_blocks.{block_index}." + _suffix_for(parent, attr, block)
-            pair = wanted.get(prefix)
-            if pair is None:
-                raise KeyError(f"pre-quantized checkpoint is missing {prefix}_nvfp4")
-            q = _QuantLinear.__new__(_QuantLinear)
-            nn.Module.__init__(q)
-            q.weight_nvfp4 = NVFP4Weight.from_packed(
-                tensors[pair[0]], tensors[pair[1]], linear.out_features, linear.in_features,
-                tensors.get(pair[0] + "_global_scale"))
-            q.in_features, q.out_features = linear.in_features, linear.out_features
-            q.calls = 0
-            if isinstance(parent, (nn.ModuleList, nn.Sequential)):
-                parent[int(attr)] = q
-            else:
-                setattr(parent, attr, q)
-            replaced += 1
+            for name in names:
+                tensors[name] = f.get_tensor(name)
+    for parent, name, key, k, n in plan:
+        weight = NVFP4Weight.from_packed(tensors[key + "_nvfp4"], tensors[key + "_nvfp4_scale"],
+                                         n, k, tensors.get(key + "_nvfp4_global_scale"))
+        _set_child(parent, name, _QuantLinear.from_weight(weight))
     torch.cuda.empty_cache()
-    return {"linears_loaded": replaced, "resident_gib": torch.cuda.memory_allocated() / 1024**3}
+    return {"linears_loaded": len(plan), "resident_gib": torch.cuda.memory_allocated() / _GIB}
 
 
 @torch.no_grad()
 def load_transformer_nvfp4(model_path: str, device: str = "cuda", model_cls=None):
-    """h3_inference/nvfp4.py:184-229.  ``model_cls`` defaults to the
-    reference's ``H3Transformer3DModel`` (imported lazily)."""
+    """Build the transformer from a packed checkpoint folder: the model on the
+    meta device, its dense tensors loaded in place (fp32 for the model's
+    ``KEEP_IN_FP32`` names, bf16 otherwise), the RoPE frequencies rebuilt from
+    the config, then ``load_quantized`` for the block linears; fails if any
+    parameter stays on the meta device (h3_inference/nvfp4.py:184-229).
+    ``model_cls`` defaults to the reference's ``H3Transformer3DModel``
+    (imported lazily)."""
     import json
     from pathlib import Path
 
@@ -386,47 +449,47 @@ def load_transformer_nvfp4(model_path: str, device: str = "cuda", model_cls=None
 
     if model_cls is None:
         from h3_inference.transformer.model import H3Transformer3DModel as model_cls
-    folder = Path(model_path) / "transformer" if (Path(model_path) / "transformer").is_dir() \
-        else Path(model_path)
-    config = {k: v for k, v in json.loads((folder / "config.json").read_text()).items()
-              if not k.startswith("_")}
+    root = Path(model_path)
+    folder = root / "transformer" if (root / "transformer").is_dir() else root
+    raw = json.loads((folder / "config.json").read_text())
+    config = {k: v for k, v in raw.items() if not k.startswith("_")}
     with torch.device("meta"):
         model = model_cls(**config)
     model.eval()
     model.requires_grad_(False)
-    keep_fp32 = getattr(model_cls, "KEEP_IN_FP32", ())
-    index = json.loads((folder / "model.safetensors.index.json").read_text())["weight_map"]
-    state: dict[str, torch.Tensor] = {}
-    for shard in sorted(set(index.values())):
+
+    fp32_names = tuple(getattr(model_cls, "KEEP_IN_FP32", ()))
+    weight_map = json.loads((folder / "model.safetensors.index.json").read_text())["weight_map"]
+    dense: dict[str, torch.Tensor] = {}
+    for shard in sorted(set(weight_map.values())):
         with safe_open(str(folder / shard), framework="pt", device=str(device)) as f:
             for name in f.keys():
-                if name.endswith(("_nvfp4", "_nvfp4_scale", "_nvfp4_global_scale")):
+                if name.endswith(_PACKED_SUFFIXES):
                     continue
-                dtype = torch.float32 if any(m in name for m in keep_fp32) else torch.bfloat16
-                state[name] = f.get_tensor(name).to(dtype)
-    model.load_state_dict(state, strict=False, assign=True)
-    del state
-    rope_theta = float(config.get("rope_theta", 10000.0))
-    rope_freq_dim = int(config.get("rope_freq_dim", 16))
-    model.rope.register_buffer(
-        "inv_freq",
-        1.0 / (rope_theta ** (torch.arange(0, 2 * rope_freq_dim, 2, dtype=torch.float32,
-                                           device=device) / (2 * rope_freq_dim))),
-        persistent=False,
-    )
+                keep = any(tag in name for tag in fp32_names)
+                dense[name] = f.get_tensor(name).to(torch.float32 if keep else torch.bfloat16)
+    model.load_state_dict(dense, strict=False, assign=True)
+    dense.clear()
+
+    theta = float(config.get("rope_theta", 10000.0))
+    half = int(config.get("rope_freq_dim", 16))
+    exponents = torch.arange(half, dtype=torch.float32, device=device) / half
+    model.rope.register_buffer("inv_freq", 1.0 / torch.pow(theta, exponents), persistent=False)
+
     summary = load_quantized(model, str(folder))
-    stranded = [n for n, p in model.named_parameters() if p.is_meta]
-    if stranded:
-        raise RuntimeError(f"Parameters left on the meta device after NVFP4 load: {stranded[:8]}")
+    left = [n for n, p in model.named_parameters() if p.is_meta]
+    if left:
+        raise RuntimeError(f"Parameters left on the meta device after NVFP4 load: {left[:8]}")
     return model, summary
 
 
 def _fused_qkv(to_q, to_k, to_v):
     """The three packed weights concatenated along N (cached on ``to_q``);
     each keeps its own global scale through the GEMM's per-segment gsB."""
+    ws = tuple(as_nvfp4_weight(m.weight_nvfp4) for m in (to_q, to_k, to_v))
+    tag = tuple(w.qdata_t.data_ptr() for w in ws)
     cached = getattr(to_q, "_h3b_fused_qkv", None)
-    ws = (to_q.weight_nvfp4, to_k.weight_nvfp4, to_v.weight_nvfp4)
-    if cached is not None and cached[0] == tuple(id(w) for w in ws):
+    if cached is not None and cached[0] == tag:
         return cached[1]
     n = ws[0].out_features
     if any(w.out_features != n or w.in_features != ws[0].in_features for w in ws) or n % 128:
@@ -435,21 +498,23 @@ def _fused_qkv(to_q, to_k, to_v):
         fused = (torch.cat([w.qdata for w in ws]), torch.cat([w.scale_u8 for w in ws]),
                  torch.cat([w.global_scale for w in ws]), n)
     try:
-        object.__setattr__(to_q, "_h3b_fused_qkv", (tuple(id(w) for w in ws), fused))
-    except Exception:
+        object.__setattr__(to_q, "_h3b_fused_qkv", (tag, fused))
+    except (AttributeError, TypeError):
         pass
     return fused
 
 
 def shared_qkv(to_q, to_k, to_v, x: torch.Tensor):
-    """One activation quantization shared by q, k, v (h3_inference/nvfp4.py:295-302).
-    Returns ``None`` unless all three are ``_QuantLinear``."""
+    """q, k and v projections from ONE quantization of ``x``
+    (h3_inference/nvfp4.py:295-302): None unless all three modules carry an
+    NVFP4 weight -- this library's ``_QuantLinear`` or the reference's own --
+    else one N-concatenated GEMM (or three when the shapes do not fuse)."""
     mods = (to_q, to_k, to_v)
-    if not all(isinstance(m, _QuantLinear) for m in mods):
+    if not all(_is_quant_linear(m) for m in mods):
         return None
     act = QuantizedActivation(x)
     for m in mods:
-        m.calls += 1
+        m.calls = getattr(m, "calls", 0) + 1
     fused = _fused_qkv(to_q, to_k, to_v)
     if fused is None:
         return tuple(act.mm(m.weight_nvfp4) for m in mods)
@@ -462,7 +527,7 @@ def shared_qkv(to_q, to_k, to_v, x: torch.Tensor):
 
 
 def report(model) -> str:
-    """h3_inference/nvfp4.py:304-307."""
-    served = sum(m.calls for m in model.modules() if isinstance(m, _QuantLinear))
-    count = sum(1 for m in model.modules() if isinstance(m, _QuantLinear))
-    return f"{count} NVFP4 linears, {served} calls served"
+    """Count of NVFP4 linears and of the calls they served
+    (h3_inference/nvfp4.py:304-307)."""
+    calls = [m.calls for m in model.modules() if isinstance(m, _QuantLinear)]
+    return f"{len(calls)} NVFP4 linears, {sum(calls)} calls served"

@@ -9,7 +9,10 @@ from __future__ import annotations
 
 import torch
 
-from . import _lib
+from . import _lib  # noqa: F401  (loaded by the operators; kept for callers of ops._lib)
+from . import torch_ops  # noqa: F401  (registers torch.ops.h3b.*)
+
+_H3B = torch.ops.h3b
 
 SF_ROWMAJOR = 0
 SF_SWIZZLED = 1
@@ -36,14 +39,6 @@ def swiglu_rows(ffn_dim: int) -> torch.Tensor:
             idx.extend(range(ffn_dim + base, ffn_dim + base + 64))
     return torch.tensor(idx, dtype=torch.long)
 M_ALIGN = 128
-
-
-def _p(t: torch.Tensor | None):
-    return None if t is None else t.data_ptr()
-
-
-def _stream(dev: torch.device) -> int:
-    return torch.cuda.current_stream(dev).cuda_stream
 
 
 def _need_cuda(*ts: torch.Tensor | None) -> torch.device:
@@ -80,8 +75,7 @@ def amax(x: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
         x2 = x2.contiguous()
     if out is None:
         out = torch.empty(1, dtype=torch.float32, device=dev)
-    _lib.check(_lib.lib().h3b_amax_bf16(_p(x2), x2.shape[0], x2.shape[1], x2.stride(0), _p(out),
-                                        _stream(dev)), "h3b_amax_bf16")
+    _H3B.amax_bf16(x2, x2.shape[0], x2.shape[1], x2.stride(0), out)
     return out
 
 
@@ -115,11 +109,8 @@ def quantize(x: torch.Tensor, *, mpad: int | None = None, layout: int = SF_SWIZZ
         raise ValueError("output buffers too small")
     if gs is None and amax_t is None:
         amax_t = amax(x2)
-    lib = _lib.lib()
-    st = lib.h3b_nvfp4_quantize(_p(x2), M, K, x2.stride(0), _p(amax_t) if gs is None else None,
-                                float(gs if gs is not None else 0.0), _p(gs_out), _p(q_out),
-                                _p(sf_out), layout, Mp, _stream(dev))
-    _lib.check(st, "h3b_nvfp4_quantize")
+    _H3B.nvfp4_quantize(x2, M, K, x2.stride(0), amax_t if gs is None else None,
+                        float(gs if gs is not None else 0.0), q_out, sf_out, gs_out, layout, Mp)
     return q_out, sf_out, gs_out
 
 
@@ -130,9 +121,7 @@ def dequantize(q: torch.Tensor, sf: torch.Tensor, gs: torch.Tensor | None, M: in
     rows = sf_rows if sf_rows is not None else (q.shape[0] if q.dim() == 2 else M)
     if out is None:
         out = torch.empty(M, K, dtype=torch.bfloat16, device=dev)
-    st = _lib.lib().h3b_nvfp4_dequantize(_p(q), _p(sf), layout, rows, _p(gs), M, K, _p(out),
-                                         _stream(dev))
-    _lib.check(st, "h3b_nvfp4_dequantize")
+    _H3B.nvfp4_dequantize(q, sf, layout, rows, gs, M, K, out)
     return out
 
 
@@ -168,11 +157,8 @@ def gemm(qa: torch.Tensor, sfa: torch.Tensor, gsa: torch.Tensor | None, M: int,
         raise ValueError("gate must be a contiguous bf16 [rows, N] table")
     if gate_idx is not None and gate_idx.dtype != torch.int32:
         gate_idx = gate_idx.to(torch.int32)
-    st = _lib.lib().h3b_nvfp4_gemm(_p(qa), _p(sfa), _p(gsa), M, a_rows, _p(qb), _p(sfb),
-                                   _p(gsb), gsb_seg, N, K, _p(bias), _p(residual), ldr,
-                                   _p(gate), _p(gate_idx), act, _p(out), out.stride(0),
-                                   _p(amax_out), _stream(dev))
-    _lib.check(st, "h3b_nvfp4_gemm")
+    _H3B.nvfp4_gemm(qa, sfa, gsa, M, qb, sfb, gsb, gsb_seg, N, K, bias, residual, ldr, gate,
+                    gate_idx, act, out, amax_out)
     return out
 
 
@@ -209,16 +195,12 @@ def rmsnorm_quantize(x: torch.Tensor, gamma: torch.Tensor, eps: float, *,
     y = buf("y", M * K, torch.bfloat16).view(M, K) if return_y else None
     if mod_idx is not None and mod_idx.dtype != torch.int32:
         mod_idx = mod_idx.to(torch.int32)
-    lib = _lib.lib()
-    s = _stream(dev)
-    _lib.check(lib.h3b_rmsnorm_stats(_p(x2), M, K, x2.stride(0), _p(gamma), float(eps), _p(shift),
-                                     _p(scale), _p(mod_idx), _p(rstd), _p(am), s),
-               "h3b_rmsnorm_stats")
+    _H3B.rmsnorm_stats(x2, M, K, x2.stride(0), gamma, float(eps), shift, scale, mod_idx, rstd,
+                       am)
     if amax_hook is not None:
         amax_hook(am)
-    _lib.check(lib.h3b_rmsnorm_quantize(_p(x2), M, K, x2.stride(0), _p(gamma), _p(shift), _p(scale),
-                                        _p(mod_idx), _p(rstd), _p(am), _p(gs), _p(q), _p(sf), Mp,
-                                        _p(y), s), "h3b_rmsnorm_quantize")
+    _H3B.rmsnorm_quantize(x2, M, K, x2.stride(0), gamma, shift, scale, mod_idx, rstd, am, gs, q,
+                          sf, Mp, y)
     return (q, sf, gs, y) if return_y else (q, sf, gs)
 
 
@@ -249,14 +231,11 @@ def qk_norm_rope(qkv: torch.Tensor, heads: int, head_dim: int, *, q_off: int, k_
         cos = cos.reshape(T, -1)
         sin = sin.reshape(T, -1)
         if (cos.stride(-1) != 1 or sin.stride(-1) != 1 or cos.stride(0) != sin.stride(0)
-                or cos.stride(0) % 4 or cos.data_ptr() % 16 or sin.data_ptr() % 16):
+                or cos.stride(0) % 4 or cos.storage_offset() % 4 or sin.storage_offset() % 4):
             cos, sin = cos.contiguous().clone(), sin.contiguous().clone()
         R, cs = cos.shape[1], cos.stride(0)
-    st = _lib.lib().h3b_qk_norm_rope(_p(q2) if heads_q else None, q2.stride(0), q_off,
-                                     _p(k2) if heads_k else None, k2.stride(0), k_off, T,
-                                     heads, head_dim, _p(wq), _p(wk), float(eps), _p(cos),
-                                     _p(sin), R, cs, _stream(dev))
-    _lib.check(st, "h3b_qk_norm_rope")
+    _H3B.qk_norm_rope(q2, q2.stride(0), q_off, None if k2 is q2 else k2, k2.stride(0), k_off, T,
+                      heads, head_dim, wq, wk, float(eps), cos, sin, R, cs, heads_q, heads_k)
     return qkv
 
 
@@ -272,8 +251,6 @@ def attention_varlen(qkv: torch.Tensor, heads: int, head_dim: int, cu_seqlens, *
     sequence (token-sharded runs: ``qkv`` is the local shard whose first row is
     global row ``q_row0``).  ``cu_seqlens``: host sequence of global document
     boundaries.  Returns ``[rows, heads*head_dim]`` bf16."""
-    import ctypes
-
     dev = _need_cuda(qkv, out, kv)
     q2 = qkv.reshape(-1, qkv.shape[-1]) if qkv.dim() != 2 else qkv
     kv2 = q2 if kv is None else (kv.reshape(-1, kv.shape[-1]) if kv.dim() != 2 else kv)
@@ -282,13 +259,9 @@ def attention_varlen(qkv: torch.Tensor, heads: int, head_dim: int, cu_seqlens, *
             raise ValueError("q / kv buffers must be bf16 with a contiguous last dim")
     rows = q2.shape[0]
     cu = [int(v) for v in (cu_seqlens.tolist() if hasattr(cu_seqlens, "tolist") else cu_seqlens)]
-    arr = (ctypes.c_int32 * len(cu))(*cu)
     if out is None:
         out = torch.empty(rows, heads * head_dim, dtype=torch.bfloat16, device=dev)
     sc = float(scale) if scale is not None else head_dim ** -0.5
-    st = _lib.lib().h3b_attention_varlen(_p(q2), rows, q2.stride(0), q_off, q_row0, _p(kv2),
-                                         kv2.shape[0], kv2.stride(0), k_off, v_off, heads,
-                                         head_dim, arr, len(cu) - 1, sc, _p(out), out.stride(0),
-                                         _stream(dev))
-    _lib.check(st, "h3b_attention_varlen")
+    _H3B.attention_varlen(q2, rows, q2.stride(0), q_off, q_row0, kv2, kv2.shape[0], kv2.stride(0),
+                          k_off, v_off, heads, head_dim, cu, sc, out)
     return out

@@ -85,9 +85,13 @@ class ParallelLayout:
         group = self.token_group
 
         def all_gather(full: torch.Tensor, local: torch.Tensor) -> None:
-            # full: [>= chunk * P, C] buffer; this rank's chunk starts at row0
+            # full: [>= chunk * P, C] buffer.  The send buffer is always this
+            # rank's in-place slot token_rank * chunk (row0 equals it except
+            # for trailing empty shards, where split_rows clamps row0 to the
+            # total and a slice at row0 would overlap another rank's slot).
             dst = full[: chunk * self.token_parallel]
-            src = dst[row0: row0 + chunk]
+            slot = self.token_rank * chunk
+            src = dst[slot: slot + chunk]
             dist.all_gather_into_tensor(dst, src, group=group)
 
         def reduce_max(t: torch.Tensor) -> None:

@@ -101,7 +101,8 @@ H3B_API int h3b_nvfp4_dequantize(const void* q, const void* sf, int sf_layout, i
  *   epilogue, in order: v = acc*alpha; v += bias[n] (bf16, optional);
  *   v = act(v); v *= gate[gate_idx[m], n] (bf16 [rows, N], optional; NULL
  *   gate_idx means row 0 -- the adaLN-zero gate of gate_residual,
- *   h3_inference/kernels/elementwise_norm_rope.py:150-163);
+ *   h3_inference/kernels/elementwise_norm_rope.py:150-163; every gate_idx[m]
+ *   must be >= 0 and below the gate table's row count, it is not checked);
  *   v += residual[m, n] (bf16, row stride ldr, optional);
  *   D = bf16(v); amax_out (optional) is atomically max-reduced with |D|
  *   (the caller zeroes it first).
@@ -127,6 +128,9 @@ H3B_API int h3b_nvfp4_gemm(const void* A, const void* sfA, const float* gsA, int
  *   y[m, k] = bf16( x*rstd*gamma[k] * (1 + scale[idx[m], k]) + shift[idx[m], k] )
  *   rstd[m] = 1 / sqrt(mean_k x[m,k]^2 + eps)
  * (modulation optional: shift/scale NULL; idx NULL means table row 0).
+ * Every idx[m] must be >= 0 and below the number of rows of the shift / scale
+ * tables: the kernels index the tables with it unchecked (the same holds
+ * for gate_idx and the gate table of h3b_nvfp4_gemm).
  * K % 256 == 0.  Pass 1 writes rstd [M] and amax_out = max|y| (zeroed on
  * `stream` first); pass 2 recomputes y and writes E2M1 codes [Mpad, K/2] and
  * swizzled scales with gs = amax / 2688 (Mpad % 128 == 0), plus y itself
@@ -190,7 +194,8 @@ H3B_API int h3b_attention_varlen(const void* q_buf, int64_t q_rows, int64_t q_st
  * until the process exits); the call itself allocates nothing.
  *   M <= 131072 rows, else H3B_ERR_INVALID_ARG; other limits as above.
  *   The first call on a device looks up the array's device address (once per
- *   device, with that device current); make that first call before any stream
+ *   device and context, with that device current; a device reset makes the
+ *   next call look it up again); make that first call before any stream
  *   capture.
  *   All calls on a device share the array: calls that overlap on the GPU
  *   race.  Order them (one stream, or events) if more than one can be in

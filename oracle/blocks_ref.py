@@ -200,3 +200,143 @@ def swiglu_ffn_block_mod(x, gamma, eps, wupq, wdownq, shift=None, scale=None, ga
         y = y * R.bf16_round(gate).astype(np.float64)[idx]
     y = y + x.astype(np.float64)
     return R.bf16_round(y.astype(np.float32)), u
+
+
+# ----------------------------------------------------------------------------- full-size row samples
+# The configured sub-block sizes (33784 or 2 x 33784 tokens, hidden 3072) are
+# too large for the fp64 helpers above on every row, but attention needs the
+# keys and values of every row of a document.  These helpers compute the
+# key / value projections of ALL rows (recipe-quantized activations and
+# weights, decoded exactly to fp32, one fp32 GEMM on the host's cores --
+# relative error ~1e-6 against the fp64 path, far inside the 1e-2 bar) and
+# everything query-side only for a sample of rows, in fp64 as above.
+
+def _row_chunks(n: int, chunk: int = 4096):
+    for a in range(0, n, chunk):
+        yield a, min(n, a + chunk)
+
+
+def rmsnorm_all(x, gamma, eps, shift=None, scale=None, mod_idx=None) -> np.ndarray:
+    """``rmsnorm`` over every row, in row chunks (bounded fp64 temporaries)."""
+    out = np.empty(x.shape, dtype=np.float32)
+    for a, b in _row_chunks(x.shape[0]):
+        idx = None if mod_idx is None else np.asarray(mod_idx)[a:b]
+        out[a:b] = rmsnorm(x[a:b], gamma, eps, shift, scale, idx)
+    return out
+
+
+def _decoded_weight_f32(w):
+    """(q, sf_rowmajor, gs) -> fp32 torch [N, K] holding LUT[code] * s (exact),
+    and gs separately."""
+    import torch
+    q, s, g = w
+    return torch.from_numpy(R.dequantize_f32(q, s, np.float32(1.0))), np.float32(g)
+
+
+def project_all_rows(h, gs_h, weights, chunk: int = 4096):
+    """bf16 ``h`` [T, K] quantized with the fixed global scale ``gs_h`` (so
+    row chunks quantize exactly as the whole tensor would), times each weight
+    triple: returns one fp32 [T, N] array of bf16 values per weight."""
+    import torch
+    dec = [_decoded_weight_f32(w) for w in weights]
+    outs = [np.empty((h.shape[0], d.shape[0]), dtype=np.float32) for d, _ in dec]
+    for a, b in _row_chunks(h.shape[0], chunk):
+        qa, sa, ga = R.quantize(h[a:b], gs=gs_h)
+        A = torch.from_numpy(R.dequantize_f32(qa, sa, np.float32(1.0)))
+        for o, (Wd, gw) in zip(outs, dec):
+            y = (A @ Wd.T).numpy().astype(np.float64) * (float(ga) * float(gw))
+            o[a:b] = R.bf16_round(y.astype(np.float32))
+    return outs
+
+
+def attention_rows(q_rows, rows, k, v, cu_seqlens, scale: float | None = None) -> np.ndarray:
+    """``attention`` for the query rows ``rows`` (``q_rows`` [S, H, D]) against
+    the full ``k``, ``v`` [T, H, D]: fp64, one BLAS product per head and row
+    group of a document."""
+    q_rows = np.asarray(q_rows, dtype=np.float64)
+    S, H, D = q_rows.shape
+    sc = D ** -0.5 if scale is None else scale
+    out = np.zeros((S, H, D))
+    cu = list(cu_seqlens)
+    doc = np.searchsorted(cu, np.asarray(rows), side="right") - 1
+    for d in np.unique(doc):
+        sel = np.nonzero(doc == d)[0]
+        a, b = cu[d], cu[d + 1]
+        for hh in range(H):
+            kh = np.asarray(k[a:b, hh], dtype=np.float64)
+            vh = np.asarray(v[a:b, hh], dtype=np.float64)
+            s = q_rows[sel, hh] @ kh.T * sc
+            s -= s.max(axis=1, keepdims=True)
+            p = np.exp(s)
+            p /= p.sum(axis=1, keepdims=True)
+            out[sel, hh] = p @ vh
+    return out
+
+
+def attn_block_rows(x, rows, gamma, eps, wq, wk, wv, wo, norm_q, norm_k, qk_eps, heads, cos,
+                    sin, cu_seqlens, gs_o, shift=None, scale=None, gate=None, mod_idx=None):
+    """``attn_block`` for the output rows ``rows`` of a full-size packed
+    sequence ``x`` [T, d].  Keys and values are computed for every row (the
+    norm's global scale is the whole tensor's, as in ``attn_block``); the
+    attention output exists only for the sampled rows here, so its
+    re-quantization uses the given global scale ``gs_o`` (the amax of the full
+    output comes from the run being checked).  Returns the sampled rows."""
+    x = R.bf16_round(x)
+    rows = np.asarray(rows)
+    T = x.shape[0]
+    h = rmsnorm_all(x, gamma, eps, shift, scale, mod_idx)
+    gs_h = R.global_scale(np.max(np.abs(h)))
+    k, v = project_all_rows(h, gs_h, (wk, wv))
+    HD = k.shape[1]
+    D = HD // heads
+    k = k.reshape(T, heads, D)
+    for a, b in _row_chunks(T):
+        k[a:b] = qk_norm_rope(k[a:b], norm_k, qk_eps, cos[a:b], sin[a:b])
+    v = v.reshape(T, heads, D)
+    hs = h[rows]
+    qa, sa, ga = R.quantize(hs, gs=gs_h)
+    qs = R.bf16_round(R.gemm_ref(qa, sa, ga, *wq, M=len(rows), N=HD).astype(np.float32))
+    qs = qk_norm_rope(qs.reshape(len(rows), heads, D), norm_q, qk_eps, cos[rows], sin[rows])
+    o = R.bf16_round(attention_rows(qs, rows, k, v, cu_seqlens).astype(np.float32))
+    qo, so, go = R.quantize(o.reshape(len(rows), HD), gs=gs_o)
+    y = R.gemm_ref(qo, so, go, *wo, M=len(rows), N=wo[0].shape[0])
+    if gate is not None:
+        idx = np.zeros(T, dtype=np.int64) if mod_idx is None else np.asarray(mod_idx)
+        y = y * R.bf16_round(gate).astype(np.float64)[idx[rows]]
+    y = y + x[rows].astype(np.float64)
+    return R.bf16_round(y.astype(np.float32)), gs_h
+
+
+def ffn_block_rows(x_rows, row_idx, gamma, eps, w1q, b1, w2q, b2, gs_h, gs_u, shift=None,
+                   scale=None, gate=None):
+    """``ffn_block_mod`` on a sample of rows (``row_idx`` their modulation
+    rows), with both activation quantizations at given global scales (the
+    amaxes of the full tensors come from the run being checked)."""
+    x = R.bf16_round(x_rows)
+    h = rmsnorm(x, gamma, eps, shift, scale, row_idx)
+    u, _ = nvfp4_linear_from_bf16(h, *w1q, bias=b1, act="gelu_tanh", gs_a=gs_h)
+    qa, sa, ga = R.quantize(u, gs=gs_u)
+    y = R.gemm_ref(qa, sa, ga, *w2q, M=x.shape[0], N=w2q[0].shape[0])
+    if b2 is not None:
+        y = y + R.bf16_round(b2).astype(np.float64)[None, :]
+    if gate is not None:
+        idx = np.zeros(x.shape[0], dtype=np.int64) if row_idx is None else np.asarray(row_idx)
+        y = y * R.bf16_round(gate).astype(np.float64)[idx]
+    y = y + x.astype(np.float64)
+    return R.bf16_round(y.astype(np.float32))
+
+
+def drift(ref, cand) -> dict:
+    """The trajectory drift metrics of ``h3_inference/tests/equiv.py:82-95``:
+    max |d|, relative L2 (%), cosine, and PSNR with the reference's
+    peak-to-peak range as the peak."""
+    a = np.asarray(ref, dtype=np.float64).ravel()
+    b = np.asarray(cand, dtype=np.float64).ravel()
+    d = b - a
+    mse = float(np.mean(d * d))
+    peak = float(a.max() - a.min())
+    psnr = float("inf") if mse == 0.0 else 20.0 * np.log10(peak) - 10.0 * np.log10(mse)
+    return {"max_abs": float(np.abs(d).max()),
+            "rel_l2_pct": 100.0 * float(np.linalg.norm(d) / np.linalg.norm(a)),
+            "cosine": float(a @ b / (np.linalg.norm(a) * np.linalg.norm(b))),
+            "psnr_db": psnr}

@@ -64,10 +64,17 @@ def pad_m(m: int) -> int:
 def bf16_round(a) -> np.ndarray:
     """fp32 -> nearest-even bf16, returned as the fp32 value it represents."""
     f = np.ascontiguousarray(a, dtype=np.float32)
-    u = f.view(np.uint32).astype(np.uint64)
-    u = (u + 0x7FFF + ((u >> 16) & 1)) & 0xFFFF0000
-    out = u.astype(np.uint32).view(np.float32)
-    return np.where(np.isnan(f), f, out)
+    u = f.view(np.uint32)
+    # uint32 arithmetic: finite values and infinities never carry out of 32
+    # bits (at most 0xFF7FFFFF + 0x8000); only NaN payloads can, and those are
+    # restored below
+    r = (u >> np.uint32(16)) & np.uint32(1)
+    r += np.uint32(0x7FFF)
+    r += u
+    r &= np.uint32(0xFFFF0000)
+    out = r.view(np.float32)
+    nan = np.isnan(f)
+    return np.where(nan, f, out) if nan.any() else out
 
 
 def bf16_bits(a) -> np.ndarray:

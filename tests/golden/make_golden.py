@@ -1,6 +1,6 @@
 """Regenerate the committed golden fixtures in this folder.
 
-    python tests/golden/make_golden.py [--reference /path/to/h3-engine]
+    python tests/golden/make_golden.py --reference /path/to/h3-engine
 
 Run in a container where the reference checkout is present (it is read, never
 modified).  What comes from where:
@@ -25,6 +25,7 @@ modified).  What comes from where:
 from __future__ import annotations
 
 import argparse
+import os
 import sys
 import types
 from pathlib import Path
@@ -212,8 +213,11 @@ def ref_block_case(ref_root: Path) -> dict[str, np.ndarray]:
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", default=os.environ.get("H3_REFERENCE_ROOT"),
+                    help="checkout of shauray8/h3-engine (or set H3_REFERENCE_ROOT)")
     args = ap.parse_args()
+    if not args.reference:
+        ap.error("give --reference or set H3_REFERENCE_ROOT to the reference checkout")
     ref_root = Path(args.reference)
     np.savez_compressed(HERE / "nvfp4_golden.npz", **nvfp4_cases(ref_root))
     np.savez_compressed(HERE / "blocks_golden.npz", **block_cases(ref_root))

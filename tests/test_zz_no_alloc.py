@@ -69,3 +69,36 @@ def test_noalloc_matches_allocating_entry_points_twice(cuda):
         assert gs.item() == rgs.item()
         assert torch.equal(q, rq)
         assert torch.equal(sf, rsf)
+
+
+@pytest.mark.gpu
+def test_noalloc_layout_edges(cuda):
+    """The two edges of the fixed array: the largest legal row count (the amax
+    slot right after the last per-row entry), compared bit for bit with the
+    allocating entry points; and no rows at all with padding rows only (the
+    padded codes and scales come out zero)."""
+    g = torch.Generator().manual_seed(22)
+    M, K = NOALLOC_MAX_ROWS, 256
+    x = torch.randn(M, K, generator=g).to(torch.bfloat16).to(cuda)
+    gamma = (1 + 0.1 * torch.randn(K, generator=g)).to(torch.bfloat16).to(cuda)
+    for _ in range(2):
+        q, sf, gs = _noalloc(x, gamma, 1e-6)
+        rq, rsf, rgs = ops.rmsnorm_quantize(x, gamma, 1e-6)
+        torch.cuda.synchronize()
+        assert gs.item() == rgs.item()
+        assert torch.equal(q, rq)
+        assert torch.equal(sf, rsf)
+    del x, q, sf, rq, rsf
+
+    K = 512
+    g0 =torch.ones(K, dtype=torch.bfloat16, device=cuda)
+    q = torch.full((128, K // 2), 0xAB, dtype=torch.uint8, device=cuda)
+    sf = torch.full((128 * (K // 16),), 0xCD, dtype=torch.uint8, device=cuda)
+    gs = torch.zeros(1, dtype=torch.float32, device=cuda)
+    st = _lib.lib().h3b_rmsnorm_quantize_noalloc(
+        None, 0, K, K, g0.data_ptr(), 1e-6, None, None, None, gs.data_ptr(), q.data_ptr(),
+        sf.data_ptr(), 128, torch.cuda.current_stream().cuda_stream)
+    _lib.check(st, "h3b_rmsnorm_quantize_noalloc")
+    torch.cuda.synchronize()
+    assert int(q.count_nonzero()) == 0
+    assert int(sf.count_nonzero()) == 0
