@@ -43,6 +43,16 @@ SIGNATURES: dict[str, tuple] = {
     "h3b_attention_varlen": (_i32, [_c_void_p, _i64, _i64, _i64, _i64, _c_void_p, _i64, _i64,
                                     _i64, _i64, _i32, _i32, ctypes.POINTER(ctypes.c_int32), _i32,
                                     _f32, _c_void_p, _i64, _c_void_p]),
+    "h3b_attention_qkv": (_i32, [_c_void_p, _i64, _c_void_p, _i64, _c_void_p, _i64, _i64, _i32,
+                                 _i32, ctypes.POINTER(ctypes.c_int32), _i32, _f32, _c_void_p, _i64,
+                                 _c_void_p]),
+    "h3b_qk_norm_rope_out": (_i32, [_c_void_p, _i64, _c_void_p, _i64, _c_void_p, _i64, _c_void_p,
+                                    _i64, _i64, _i32, _i32, _c_void_p, _c_void_p, _f32, _c_void_p,
+                                    _c_void_p, _i32, _i64, _c_void_p]),
+    "h3b_gate_residual": (_i32, [_c_void_p, _i64, _c_void_p, _i64, _c_void_p, _c_void_p, _i64,
+                                 _i64, _i64, _c_void_p, _i64, _c_void_p]),
+    "h3b_ada_modulate": (_i32, [_c_void_p, _i64, _c_void_p, _c_void_p, _c_void_p, _i64, _i64,
+                                _i64, _c_void_p, _i64, _c_void_p]),
     "h3b_rmsnorm_quantize_noalloc": (_i32, [_c_void_p, _i64, _i64, _i64, _c_void_p, _f32,
                                             _c_void_p, _c_void_p, _c_void_p, _c_void_p,
                                             _c_void_p, _c_void_p, _i64, _c_void_p]),

@@ -76,7 +76,8 @@ static_assert(SMEM_BYTES <= 232448, "shared memory budget");
 
 struct Args {
   CUtensorMap tmap_q;      // bf16 [q_rows, q_stride], box 64 x 128, 128B swizzle
-  CUtensorMap tmap_kv;     // bf16 [kv_rows, kv_stride], same box
+  CUtensorMap tmap_kv;     // keys: bf16 [kv_rows, k_stride], same box
+  CUtensorMap tmap_v;      // values: bf16 [kv_rows, v_stride] (often the keys' map)
   __nv_bfloat16* out;      // [q_rows, ldo]; head h at columns h*D
   long long ldo;
   int q_off, k_off, v_off; // element offsets of the q / k / v head blocks in their rows
@@ -244,6 +245,7 @@ __global__ void __launch_bounds__(THREADS, 1) k_fmha(const __grid_constant__ Arg
     if (lane == 0) {
       prefetch_tmap(&p.tmap_q);
       prefetch_tmap(&p.tmap_kv);
+      prefetch_tmap(&p.tmap_v);
       const int qx = p.q_off + head * D, kx = p.k_off + head * D, vx = p.v_off + head * D;
       uint32_t fb = smem_u32(q_full);
       mbar_expect_tx(fb, 3 * TILE_BYTES);
@@ -261,8 +263,8 @@ __global__ void __launch_bounds__(THREADS, 1) k_fmha(const __grid_constant__ Arg
         if (j < n_kv) {
           tma_prefetch_2d(&p.tmap_kv, kx, row0 + j * BK);
           tma_prefetch_2d(&p.tmap_kv, kx + 64, row0 + j * BK);
-          tma_prefetch_2d(&p.tmap_kv, vx, row0 + j * BK);
-          tma_prefetch_2d(&p.tmap_kv, vx + 64, row0 + j * BK);
+          tma_prefetch_2d(&p.tmap_v, vx, row0 + j * BK);
+          tma_prefetch_2d(&p.tmap_v, vx + 64, row0 + j * BK);
         }
       };
       for (int j = 1; j < kPrefetchTiles; ++j) prefetch(j);
@@ -284,8 +286,8 @@ __global__ void __launch_bounds__(THREADS, 1) k_fmha(const __grid_constant__ Arg
         const uint32_t b = smem_u32(&kv_full[j & 1]);
         mbar_expect_tx(b, more ? 2 * TILE_BYTES : TILE_BYTES);
         uint8_t* vdst = smem + V_OFF + (j & 1) * TILE_BYTES;
-        tma_load_2d(smem_u32(vdst), &p.tmap_kv, vx, row0 + j * BK, b);
-        tma_load_2d(smem_u32(vdst + BOX_BYTES), &p.tmap_kv, vx + 64, row0 + j * BK, b);
+        tma_load_2d(smem_u32(vdst), &p.tmap_v, vx, row0 + j * BK, b);
+        tma_load_2d(smem_u32(vdst + BOX_BYTES), &p.tmap_v, vx + 64, row0 + j * BK, b);
         if (more) {
           uint8_t* kdst = smem + K_OFF + ((j + 1) & 1) * TILE_BYTES;
           tma_load_2d(smem_u32(kdst), &p.tmap_kv, kx, row0 + (j + 1) * BK, b);

@@ -20,6 +20,7 @@
 #include "norm.cuh"
 #include "rope.cuh"
 #include "attention.cuh"
+#include "elementwise.cuh"
 
 namespace h3b {
 
@@ -204,9 +205,9 @@ int h3b_nvfp4_dequantize(const void* q, const void* sf, int sf_layout, int64_t s
   if (M == 0) return H3B_OK;
   if (!q || !sf || !out) return H3B_ERR_INVALID_ARG;
   if ((reinterpret_cast<uintptr_t>(q) & 3u) || !aligned16(out)) return H3B_ERR_ALIGNMENT;
-  const int64_t total = M * (K / 8);
-  int64_t blocks = (total + 255) / 256;
-  const int64_t cap = (int64_t)num_sms() * 16;
+  if (K / 8 > (int64_t)INT32_MAX) return H3B_ERR_INVALID_ARG;
+  int64_t blocks = (M + 7) / 8;                       // one warp per row, 8 per CTA
+  const int64_t cap = (int64_t)num_sms() * 8;
   if (blocks > cap) blocks = cap;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   auto qp = static_cast<const uint8_t*>(q);
@@ -358,10 +359,17 @@ int h3b_rmsnorm_quantize(const void* x, int64_t M, int64_t K, int64_t ldx, const
 }
 
 // ------------------------------------------------------------------ qk-norm + RoPE
-int h3b_qk_norm_rope(void* q, int64_t q_stride, int64_t q_off, void* k, int64_t k_stride,
-                     int64_t k_off, int64_t T, int H, int D, const void* wq, const void* wk,
-                     float eps, const float* cos, const float* sin, int R, int64_t cs_stride,
-                     void* stream) {
+}  // extern "C"
+
+namespace h3b {
+// Shared by the in-place and the out-of-place entry points: q / k are read at
+// (stride, off), the results written to qo / ko at (o_stride, o_off).
+static int qk_norm_rope_launch(const void* q, int64_t q_stride, int64_t q_off, const void* k,
+                               int64_t k_stride, int64_t k_off, void* qo, int64_t qo_stride,
+                               int64_t qo_off, void* ko, int64_t ko_stride, int64_t ko_off,
+                               int64_t T, int H, int D, const void* wq, const void* wk, float eps,
+                               const float* cos, const float* sin, int R, int64_t cs_stride,
+                               void* stream) {
   if (T < 0 || H <= 0 || (D != 64 && D != 128)) return H3B_ERR_INVALID_ARG;
   if (cos != nullptr) {
     // the partner of a lane's 8 columns is a whole lane away: R/2 % 8 == 0;
@@ -373,20 +381,33 @@ int h3b_qk_norm_rope(void* q, int64_t q_stride, int64_t q_off, void* k, int64_t 
     R = 0;
   }
   const int64_t hd = (int64_t)H * D;
-  if (q_off < 0 || k_off < 0 || q_off + hd > q_stride || k_off + hd > k_stride)
+  // a NULL q (or k) skips those heads: its strides and offsets are not used
+  if (q && (q_off < 0 || qo_off < 0 || q_off + hd > q_stride || qo_off + hd > qo_stride))
     return H3B_ERR_INVALID_ARG;
-  if ((q_stride | k_stride | q_off | k_off) % 8) return H3B_ERR_ALIGNMENT;
+  if (k && (k_off < 0 || ko_off < 0 || k_off + hd > k_stride || ko_off + hd > ko_stride))
+    return H3B_ERR_INVALID_ARG;
+  if ((q && (q_stride | q_off | qo_stride | qo_off) % 8) ||
+      (k && (k_stride | k_off | ko_stride | ko_off) % 8))
+    return H3B_ERR_ALIGNMENT;
   if (T == 0) return H3B_OK;
   if (!q && !k) return H3B_ERR_INVALID_ARG;            // NULL q or k: those heads are skipped
-  if ((q && !aligned16(q)) || (k && !aligned16(k))) return H3B_ERR_ALIGNMENT;
+  if ((q && !qo) || (k && !ko)) return H3B_ERR_INVALID_ARG;
+  if ((q && (!aligned16(q) || !aligned16(qo))) || (k && (!aligned16(k) || !aligned16(ko))))
+    return H3B_ERR_ALIGNMENT;
   RopeArgs a;
-  a.q = static_cast<__nv_bfloat16*>(q);
-  a.k = static_cast<__nv_bfloat16*>(k);
+  a.q = static_cast<const __nv_bfloat16*>(q);
+  a.k = static_cast<const __nv_bfloat16*>(k);
+  a.qo = static_cast<__nv_bfloat16*>(qo);
+  a.ko = static_cast<__nv_bfloat16*>(ko);
   a.T = T;
   a.q_stride = q_stride;
   a.k_stride = k_stride;
   a.q_off = q_off;
   a.k_off = k_off;
+  a.qo_stride = qo_stride;
+  a.ko_stride = ko_stride;
+  a.qo_off = qo_off;
+  a.ko_off = ko_off;
   a.H = H;
   a.hq = q ? H : 0;
   a.hk = k ? H : 0;
@@ -401,6 +422,21 @@ int h3b_qk_norm_rope(void* q, int64_t q_stride, int64_t q_off, void* k, int64_t 
   const int64_t cap = (int64_t)num_sms() * 8;
   if (blocks > cap) blocks = cap;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (R == D) {
+    // full-width rotary: each lane holds a column block and its rotate-half
+    // partner; head vectors per warp instruction 32 / (D / 16); 3 or 4 of
+    // them in flight per lane (4 unless only 3 divides the row's head vectors)
+    const int steps = (a.hq + a.hk) / (512 / D);
+    const bool three = steps % 4 != 0 && steps % 3 == 0;
+    if (D == 128) {
+      if (three) k_qk_norm_rope_full<128, 3><<<(unsigned)blocks, kRopeWarps * 32, 0, st>>>(a);
+      else k_qk_norm_rope_full<128, 4><<<(unsigned)blocks, kRopeWarps * 32, 0, st>>>(a);
+    } else {
+      if (three) k_qk_norm_rope_full<64, 3><<<(unsigned)blocks, kRopeWarps * 32, 0, st>>>(a);
+      else k_qk_norm_rope_full<64, 4><<<(unsigned)blocks, kRopeWarps * 32, 0, st>>>(a);
+    }
+    return launched(cudaGetLastError());
+  }
   // head vectors of a row per warp instruction: 32 lanes / (D / 8 lanes each)
   const int steps = (a.hq + a.hk) / (256 / D);
   const bool seven = steps % 6 != 0 && steps % 7 == 0;
@@ -412,6 +448,84 @@ int h3b_qk_norm_rope(void* q, int64_t q_stride, int64_t q_off, void* k, int64_t 
     else k_qk_norm_rope<64, 6><<<(unsigned)blocks, kRopeWarps * 32, 0, st>>>(a);
   }
   return launched(cudaGetLastError());
+}
+}  // namespace h3b
+
+extern "C" {
+
+int h3b_qk_norm_rope(void* q, int64_t q_stride, int64_t q_off, void* k, int64_t k_stride,
+                     int64_t k_off, int64_t T, int H, int D, const void* wq, const void* wk,
+                     float eps, const float* cos, const float* sin, int R, int64_t cs_stride,
+                     void* stream) {
+  return qk_norm_rope_launch(q, q_stride, q_off, k, k_stride, k_off, q, q_stride, q_off, k,
+                             k_stride, k_off, T, H, D, wq, wk, eps, cos, sin, R, cs_stride,
+                             stream);
+}
+
+int h3b_qk_norm_rope_out(const void* q, int64_t q_stride, const void* k, int64_t k_stride,
+                         void* q_out, int64_t qo_stride, void* k_out, int64_t ko_stride,
+                         int64_t T, int H, int D, const void* wq, const void* wk, float eps,
+                         const float* cos, const float* sin, int R, int64_t cs_stride,
+                         void* stream) {
+  return qk_norm_rope_launch(q, q_stride, 0, k, k_stride, 0, q_out, qo_stride, 0, k_out,
+                             ko_stride, 0, T, H, D, wq, wk, eps, cos, sin, R, cs_stride, stream);
+}
+
+// ------------------------------------------------------------------ gathered gate / modulation
+}  // extern "C"
+
+namespace h3b {
+static int gather_elementwise_launch(bool gate, const void* a, int64_t lda, const void* b,
+                                     int64_t ldb, const void* t0, const void* t1,
+                                     const int32_t* idx, int64_t n_idx, int64_t rows,
+                                     int64_t cols, void* out, int64_t ldo, void* stream) {
+  if (rows < 0 || cols <= 0 || cols % 8 || lda < cols || ldo < cols || n_idx < 0)
+    return H3B_ERR_INVALID_ARG;
+  if (gate && ldb < cols) return H3B_ERR_INVALID_ARG;
+  if (idx && n_idx == 0) return H3B_ERR_INVALID_ARG;
+  if ((lda | ldo | (gate ? ldb : 0)) % 8) return H3B_ERR_ALIGNMENT;
+  if (rows == 0) return H3B_OK;
+  if (!a || !t0 || !out || (gate && !b) || (!gate && !t1)) return H3B_ERR_INVALID_ARG;
+  if (!aligned16(a) || !aligned16(t0) || !aligned16(out) || (gate && !aligned16(b)) ||
+      (!gate && !aligned16(t1)))
+    return H3B_ERR_ALIGNMENT;
+  EwArgs p;
+  p.a = static_cast<const __nv_bfloat16*>(a);
+  p.b = static_cast<const __nv_bfloat16*>(b);
+  p.t0 = static_cast<const __nv_bfloat16*>(t0);
+  p.t1 = static_cast<const __nv_bfloat16*>(t1);
+  p.idx = idx;
+  p.out = static_cast<__nv_bfloat16*>(out);
+  p.rows = rows;
+  p.cols = cols;
+  p.lda = lda;
+  p.ldb = gate ? ldb : 0;
+  p.ldo = ldo;
+  p.n_idx = n_idx;
+  int64_t blocks = (rows + 7) / 8;                      // one warp per row, 8 per CTA
+  const int64_t cap = (int64_t)num_sms() * 8;
+  if (blocks > cap) blocks = cap;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (gate) k_gather_elementwise<true><<<(unsigned)blocks, 256, 0, st>>>(p);
+  else k_gather_elementwise<false><<<(unsigned)blocks, 256, 0, st>>>(p);
+  return launched(cudaGetLastError());
+}
+}  // namespace h3b
+
+extern "C" {
+
+int h3b_gate_residual(const void* residual, int64_t ldr, const void* y, int64_t ldy,
+                      const void* gate, const int32_t* idx, int64_t n_idx, int64_t rows,
+                      int64_t cols, void* out, int64_t ldo, void* stream) {
+  return gather_elementwise_launch(true, residual, ldr, y, ldy, gate, nullptr, idx, n_idx, rows,
+                                   cols, out, ldo, stream);
+}
+
+int h3b_ada_modulate(const void* x, int64_t ldx, const void* scale, const void* shift,
+                     const int32_t* idx, int64_t n_idx, int64_t rows, int64_t cols, void* out,
+                     int64_t ldo, void* stream) {
+  return gather_elementwise_launch(false, x, ldx, nullptr, 0, scale, shift, idx, n_idx, rows,
+                                   cols, out, ldo, stream);
 }
 
 // ------------------------------------------------------------------ packed varlen attention
@@ -429,11 +543,17 @@ static int tmap_bf16_rows(CUtensorMap* tm, const void* base, int64_t rows, int64
              : H3B_ERR_INVALID_ARG;
 }
 
-int h3b_attention_varlen(const void* q_buf, int64_t q_rows, int64_t q_stride, int64_t q_off,
-                         int64_t q_row0, const void* kv_buf, int64_t kv_rows, int64_t kv_stride,
-                         int64_t k_off, int64_t v_off, int H, int D,
-                         const int32_t* cu_seqlens_host, int ndocs, float scale, void* out,
-                         int64_t ldo, void* stream) {
+}  // extern "C"
+
+namespace h3b {
+// Shared by both attention entry points: queries from q_buf (q_rows local
+// rows starting at global row q_row0), keys from k_buf and values from v_buf
+// (kv_rows rows each, the whole sequence).
+static int attention_launch(const void* q_buf, int64_t q_rows, int64_t q_stride, int64_t q_off,
+                            int64_t q_row0, const void* k_buf, int64_t k_stride, int64_t k_off,
+                            const void* v_buf, int64_t v_stride, int64_t v_off, int64_t kv_rows,
+                            int H, int D, const int32_t* cu_seqlens_host, int ndocs, float scale,
+                            void* out, int64_t ldo, void* stream) {
   if (q_rows < 0 || kv_rows < 0 || q_row0 < 0 || q_row0 + q_rows > kv_rows) return H3B_ERR_INVALID_ARG;
   if (H <= 0 || D != attn::D || ndocs <= 0 || ndocs > attn::MAX_DOCS || !cu_seqlens_host)
     return H3B_ERR_INVALID_ARG;
@@ -442,16 +562,17 @@ int h3b_attention_varlen(const void* q_buf, int64_t q_rows, int64_t q_stride, in
   for (int i = 0; i < ndocs; ++i)
     if (cu_seqlens_host[i + 1] < cu_seqlens_host[i]) return H3B_ERR_INVALID_ARG;
   const int64_t hd = (int64_t)H * D;
-  if (q_off < 0 || k_off < 0 || v_off < 0 || q_off + hd > q_stride || k_off + hd > kv_stride ||
-      v_off + hd > kv_stride || ldo < hd)
+  if (q_off < 0 || k_off < 0 || v_off < 0 || q_off + hd > q_stride || k_off + hd > k_stride ||
+      v_off + hd > v_stride || ldo < hd)
     return H3B_ERR_INVALID_ARG;
-  if ((q_stride | kv_stride | q_off | k_off | v_off | ldo) % 8) return H3B_ERR_ALIGNMENT;
+  if ((q_stride | k_stride | v_stride | q_off | k_off | v_off | ldo) % 8) return H3B_ERR_ALIGNMENT;
   if (kv_rows > (int64_t)INT32_MAX - 256 || q_stride > (int64_t)INT32_MAX ||
-      kv_stride > (int64_t)INT32_MAX)
+      k_stride > (int64_t)INT32_MAX || v_stride > (int64_t)INT32_MAX)
     return H3B_ERR_INVALID_ARG;
   if (q_rows == 0) return H3B_OK;
-  if (!q_buf || !kv_buf || !out) return H3B_ERR_INVALID_ARG;
-  if (!aligned16(q_buf) || !aligned16(kv_buf) || !aligned16(out)) return H3B_ERR_ALIGNMENT;
+  if (!q_buf || !k_buf || !v_buf || !out) return H3B_ERR_INVALID_ARG;
+  if (!aligned16(q_buf) || !aligned16(k_buf) || !aligned16(v_buf) || !aligned16(out))
+    return H3B_ERR_ALIGNMENT;
   int rc = check_sm100();
   if (rc != H3B_OK) return rc;
 
@@ -473,8 +594,14 @@ int h3b_attention_varlen(const void* q_buf, int64_t q_rows, int64_t q_stride, in
   memset(&args, 0, sizeof(args));
   rc = tmap_bf16_rows(&args.tmap_q, q_buf, q_rows, q_stride);
   if (rc != H3B_OK) return rc;
-  rc = tmap_bf16_rows(&args.tmap_kv, kv_buf, kv_rows, kv_stride);
+  rc = tmap_bf16_rows(&args.tmap_kv, k_buf, kv_rows, k_stride);
   if (rc != H3B_OK) return rc;
+  if (v_buf == k_buf && v_stride == k_stride) {
+    args.tmap_v = args.tmap_kv;
+  } else {
+    rc = tmap_bf16_rows(&args.tmap_v, v_buf, kv_rows, v_stride);
+    if (rc != H3B_OK) return rc;
+  }
   args.out = static_cast<__nv_bfloat16*>(out);
   args.ldo = ldo;
   args.q_off = (int)q_off;
@@ -511,6 +638,27 @@ int h3b_attention_varlen(const void* q_buf, int64_t q_rows, int64_t q_stride, in
   attn::k_fmha<<<(unsigned)items, attn::THREADS, attn::SMEM_BYTES,
                  static_cast<cudaStream_t>(stream)>>>(args);
   return launched(cudaGetLastError());
+}
+}  // namespace h3b
+
+extern "C" {
+
+int h3b_attention_varlen(const void* q_buf, int64_t q_rows, int64_t q_stride, int64_t q_off,
+                         int64_t q_row0, const void* kv_buf, int64_t kv_rows, int64_t kv_stride,
+                         int64_t k_off, int64_t v_off, int H, int D,
+                         const int32_t* cu_seqlens_host, int ndocs, float scale, void* out,
+                         int64_t ldo, void* stream) {
+  return attention_launch(q_buf, q_rows, q_stride, q_off, q_row0, kv_buf, kv_stride, k_off,
+                          kv_buf, kv_stride, v_off, kv_rows, H, D, cu_seqlens_host, ndocs, scale,
+                          out, ldo, stream);
+}
+
+int h3b_attention_qkv(const void* q, int64_t q_stride, const void* k, int64_t k_stride,
+                      const void* v, int64_t v_stride, int64_t rows, int H, int D,
+                      const int32_t* cu_seqlens_host, int ndocs, float scale, void* out,
+                      int64_t ldo, void* stream) {
+  return attention_launch(q, rows, q_stride, 0, 0, k, k_stride, 0, v, v_stride, 0, rows, H, D,
+                          cu_seqlens_host, ndocs, scale, out, ldo, stream);
 }
 
 // ------------------------------------------------------------------ RMSNorm -> NVFP4, no allocation

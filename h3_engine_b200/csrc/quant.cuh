@@ -230,40 +230,66 @@ __global__ void __launch_bounds__(kAmaxThreads)
   block_atomic_max(m, out);
 }
 
-// Unpack: one thread per 8 codes (4 bytes) -> 8 bf16 (16 bytes).
+// Unpack: E2M1 codes (4 bytes per 8 values) and their e4m3 block scale -> 8
+// bf16 values (16 bytes), bf16((LUT[code] * s) * gs).
 template <int LAYOUT>
 __global__ void __launch_bounds__(256)
     k_nvfp4_dequantize(const uint8_t* __restrict__ q, const uint8_t* __restrict__ sf,
                        const float* __restrict__ gs_ptr, int64_t M, int64_t K,
                        __nv_bfloat16* __restrict__ out) {
+  // One warp per row (grid-stride over rows); lane l takes the 8-value halves
+  // l, l + 32, ... of the row, four in flight: 128 contiguous bytes of codes
+  // read and 512 bytes written per warp instruction, no per-element division.
   const float gs = gs_ptr ? __ldg(gs_ptr) : 1.0f;
-  const int64_t hpr = K >> 3;
-  const int64_t total = M * hpr;
+  const int lane = threadIdx.x & 31;
+  const int hpr = (int)(K >> 3);              // 8-value halves per row
   const int64_t c_row = K >> 4, c4 = K >> 6;
-  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
-  for (int64_t h = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; h < total; h += stride) {
-    const int64_t row = h / hpr, hc = h - row * hpr, c = hc >> 1;
-    const uint32_t codes = __ldg(reinterpret_cast<const uint32_t*>(q + row * (K >> 1)) + hc);
-    const int64_t off = LAYOUT == H3B_SF_SWIZZLED ? sf_swizzled_offset(row, c, c4) : row * c_row + c;
-    const float s = e4m3_to_f32(__ldg(sf + off));
-    uint32_t hx2[4];
-    asm("{\n\t.reg .b8 b0, b1, b2, b3;\n\t"
-        "mov.b32 {b0, b1, b2, b3}, %4;\n\t"
-        "cvt.rn.f16x2.e2m1x2 %0, b0;\n\t"
-        "cvt.rn.f16x2.e2m1x2 %1, b1;\n\t"
-        "cvt.rn.f16x2.e2m1x2 %2, b2;\n\t"
-        "cvt.rn.f16x2.e2m1x2 %3, b3;\n\t}"
-        : "=r"(hx2[0]), "=r"(hx2[1]), "=r"(hx2[2]), "=r"(hx2[3])
-        : "r"(codes));
-    uint32_t o[4];
+  const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  constexpr int U = 4;
+  for (int64_t row = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; row < M;
+       row += nwarps) {
+    const uint32_t* qrow = reinterpret_cast<const uint32_t*>(q + row * (K >> 1));
+    __nv_bfloat16* orow = out + row * K;
+    for (int h0 = lane; h0 < hpr; h0 += 32 * U) {
+      uint32_t codes[U];
+      uint8_t s8[U];
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&hx2[i]));
-      const float lo = __fmul_rn(__fmul_rn(f.x, s), gs);
-      const float hi = __fmul_rn(__fmul_rn(f.y, s), gs);
-      o[i] = pack_bf16x2(lo, hi);
+      for (int u = 0; u < U; ++u) {
+        const int hc = h0 + u * 32;
+        codes[u] = 0;
+        s8[u] = 0;
+        if (hc < hpr) {
+          codes[u] = __ldg(qrow + hc);
+          const int64_t c = hc >> 1;
+          s8[u] = __ldg(sf + (LAYOUT == H3B_SF_SWIZZLED ? sf_swizzled_offset(row, c, c4)
+                                                         : row * c_row + c));
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int hc = h0 + u * 32;
+        if (hc >= hpr) break;
+        const float s = e4m3_to_f32(s8[u]);
+        uint32_t hx2[4];
+        asm("{\n\t.reg .b8 b0, b1, b2, b3;\n\t"
+            "mov.b32 {b0, b1, b2, b3}, %4;\n\t"
+            "cvt.rn.f16x2.e2m1x2 %0, b0;\n\t"
+            "cvt.rn.f16x2.e2m1x2 %1, b1;\n\t"
+            "cvt.rn.f16x2.e2m1x2 %2, b2;\n\t"
+            "cvt.rn.f16x2.e2m1x2 %3, b3;\n\t}"
+            : "=r"(hx2[0]), "=r"(hx2[1]), "=r"(hx2[2]), "=r"(hx2[3])
+            : "r"(codes[u]));
+        uint32_t o[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&hx2[i]));
+          const float lo = __fmul_rn(__fmul_rn(f.x, s), gs);
+          const float hi = __fmul_rn(__fmul_rn(f.y, s), gs);
+          o[i] = pack_bf16x2(lo, hi);
+        }
+        *reinterpret_cast<uint4*>(orow + (int64_t)hc * 8) = make_uint4(o[0], o[1], o[2], o[3]);
+      }
     }
-    *reinterpret_cast<uint4*>(out + row * K + hc * 8) = make_uint4(o[0], o[1], o[2], o[3]);
   }
 }
 

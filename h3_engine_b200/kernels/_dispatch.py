@@ -13,12 +13,13 @@ reach these kernels once its plug-in import resolves to this module::
     sys.modules["maiku.dispatch"] = _dispatch
 
 Names answered (the strings the reference's shims pass):
-``rope``, ``norm_rope_h3``, ``norm_modulate_h3`` (elementwise_norm_rope.py),
-``attention`` (packed_self_attn.py), ``qkv_projection``, ``out_projection``,
-``ffn`` (ffn_qkvo_gemms.py).  ``ada_modulate_gather`` and
-``gate_residual_gather`` are MISS: this library fuses the modulation gather
+``rope``, ``norm_rope_h3``, ``norm_modulate_h3``, ``ada_modulate_gather``,
+``gate_residual_gather`` (elementwise_norm_rope.py), ``attention``
+(packed_self_attn.py), ``qkv_projection``, ``out_projection``, ``ffn``
+(ffn_qkvo_gemms.py).  The library's own blocks fuse the modulation gather
 into the RMSNorm -> NVFP4 kernel and the gate + residual into the GEMM
-epilogue of its own blocks, and has no standalone kernel for either.
+epilogue; the two gather kernels serve the reference's block, which calls
+them as separate rows.
 
 A call whose arguments the kernels do not take (CPU tensors, an attention
 mask, head_dim other than 128 for attention, rotary widths whose half is not
@@ -84,6 +85,8 @@ def _table() -> dict:
         "rope": lambda x, cos, sin: ew.rope_kernel(x, None, 0.0, cos, sin),
         "norm_rope_h3": ew.rope_kernel,
         "norm_modulate_h3": ew.norm_modulate_kernel,
+        "ada_modulate_gather": ew.ada_modulate_kernel,
+        "gate_residual_gather": ew.gate_residual_kernel,
         "attention": at.attention_kernel_flat,
         "qkv_projection": gm.qkv_kernel,
         "out_projection": gm.out_kernel,

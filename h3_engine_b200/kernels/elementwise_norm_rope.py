@@ -6,10 +6,13 @@ Same functions, signatures and env flags as the reference:
 * ``apply_rotary_emb``           -- H3_FUSED_ROPE: rotate-half RoPE kernel (:25-40)
 * ``norm_modulate``              -- H3_FUSED_MODULATE: RMSNorm + gathered
                                     shift / scale in the RMSNorm -> NVFP4 kernel (:69-88)
-* ``ada_modulate``               -- stock expression (:90-102)
+* ``ada_modulate``               -- H3_FUSED_MODULATE: gathered modulation kernel (:90-102)
 * ``norm_rope``                  -- H3_FUSED_ROPE: per-head RMSNorm + RoPE kernel (:104-148)
-* ``gate_residual``              -- stock expression (:150-163)
+* ``gate_residual``              -- H3_FUSED_GATE: gathered gate + residual kernel (:150-163)
 
+The gather kernels round to bf16 after every op as torch's bf16 expression
+does, so their results equal the stock expression's bit for bit.  The RoPE
+kernels write a new tensor (out of place) and leave the input untouched.
 Where the reference falls back to ``torch.compile`` of its expression, these
 shims run the same expression eagerly (calls the kernels do not cover).
 
@@ -48,19 +51,23 @@ def _rope_covered(x: torch.Tensor, w, cos, sin) -> bool:
 
 def rope_kernel(x: torch.Tensor, w, eps: float, cos: torch.Tensor, sin: torch.Tensor):
     """Per-head RMSNorm (``w`` not None) + rotate-half RoPE of ``x`` (B, T, H, D)
-    with tables ``cos`` / ``sin`` (T, R) on a copy of ``x``, or MISS."""
+    with tables ``cos`` / ``sin`` (T, R), into a new tensor, or MISS.  ``x``
+    may be a strided view (the q / k slices of one projection output)."""
     from h3_engine_b200 import ops
     if not _rope_covered(x, w, cos, sin):
         return MISS
     B, T, H, D = x.shape
-    out = x.contiguous().clone()
-    cs, sn = cos.float(), sin.float()
-    if B > 1:
+    try:
+        x2 = x.view(B * T, H * D)       # rows of the projection output, no copy
+    except RuntimeError:
+        x2 = x.reshape(B * T, H * D)
+    cs, sn = cos, sin
+    if B > 1:                           # per-row tables for every batch element
         cs, sn = cs.repeat(B, 1), sn.repeat(B, 1)
-    wq = None if w is None else w.detach().to(torch.bfloat16).contiguous()
-    ops.qk_norm_rope(out.view(B * T, H * D), H, D, q_off=0, k_off=0, wq=wq, wk=None,
-                     eps=float(eps), cos=cs.contiguous(), sin=sn.contiguous(), heads_k=False)
-    return out
+    wq = None if w is None else (w if w.dtype == torch.bfloat16 and w.is_contiguous()
+                                 else w.detach().to(torch.bfloat16).contiguous())
+    out = ops.qk_norm_rope_out(x2, H, D, w=wq, eps=float(eps), cos=cs, sin=sn)
+    return out.view(B, T, H, D)
 
 
 def apply_rotary_emb(hidden_states: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor) -> torch.Tensor:
@@ -104,17 +111,47 @@ def norm_modulate_kernel(x: torch.Tensor, w: torch.Tensor, eps: float, scale: to
         return MISS
     if not (w.is_cuda and scale.is_cuda and shift.is_cuda and indices.is_cuda):
         return MISS
-    idx = indices.to(torch.int32)
-    if idx.numel() != rows:
-        idx = idx.repeat(rows // idx.numel())
+    idx = _row_indices(indices, rows)
     x2 = x.reshape(rows, K)
+    # per-row scratch (rstd, amax) is reused across calls on the device's
+    # stream; the outputs are fresh, they ride on the returned tensor
+    scratch = _NORM_SCRATCH.setdefault(x.device, {})
+    ws = dict(scratch)
     q, sf, gs, y = ops.rmsnorm_quantize(
-        x2, w.detach().to(torch.bfloat16).contiguous(), float(eps),
-        shift=shift.to(torch.bfloat16).contiguous(), scale=scale.to(torch.bfloat16).contiguous(),
-        mod_idx=idx.contiguous(), return_y=True, ws={})
+        x2, _bf16(w), float(eps), shift=_bf16(shift), scale=_bf16(scale), mod_idx=idx,
+        return_y=True, ws=ws)
+    scratch["rstd"], scratch["amax"] = ws["rstd"], ws["amax"]
     y = y.view(x.shape)
     y._h3b_nvfp4 = (q, sf, gs, y._version)
     return y
+
+
+_NORM_SCRATCH: dict = {}
+_IDX_CACHE: dict = {}
+
+
+def _bf16(t: torch.Tensor) -> torch.Tensor:
+    """``t`` as contiguous bf16 (itself when it already is)."""
+    t = t.detach()
+    return t if t.dtype == torch.bfloat16 and t.is_contiguous() else t.to(torch.bfloat16).contiguous()
+
+
+def _row_indices(indices: torch.Tensor, rows: int) -> torch.Tensor:
+    """int32 table row per activation row (``indices`` repeated over the
+    batch), converted once per indices tensor: the model passes the same
+    per-token table indices to every block."""
+    key = (indices.device, indices.data_ptr(), indices._version, indices.numel(), rows)
+    hit = _IDX_CACHE.get(key)
+    if hit is not None and hit[0] is indices:
+        return hit[1]
+    idx = indices.to(torch.int32)
+    if idx.numel() != rows:
+        idx = idx.repeat(rows // idx.numel())
+    idx = idx.contiguous()
+    if len(_IDX_CACHE) > 64:
+        _IDX_CACHE.clear()
+    _IDX_CACHE[key] = (indices, idx)
+    return idx
 
 
 def norm_modulate(norm_module: nn.RMSNorm, x: torch.Tensor, scale: torch.Tensor,
@@ -132,9 +169,51 @@ def norm_modulate(norm_module: nn.RMSNorm, x: torch.Tensor, scale: torch.Tensor,
     return _norm_modulate_impl(x, w, float(norm_module.eps), scale, shift, indices)
 
 
+def _gather_covered(a: torch.Tensor, tables, indices: torch.Tensor) -> bool:
+    if not all(isinstance(t, torch.Tensor) for t in (a, indices, *tables)):
+        return False
+    if not (a.is_cuda and a.dtype == torch.bfloat16 and a.dim() >= 2 and a.shape[-1] % 8 == 0):
+        return False
+    C = a.shape[-1]
+    if not all(t.is_cuda and t.dtype == torch.bfloat16 and t.dim() == 2 and t.shape[-1] == C
+               for t in tables):
+        return False
+    rows = a.numel() // C
+    return (indices.is_cuda and indices.dim() == 1 and indices.numel() > 0
+            and rows % indices.numel() == 0 and (a.dim() < 3 or a.shape[-2] == indices.numel()))
+
+
+def ada_modulate_kernel(normed: torch.Tensor, scale: torch.Tensor, shift: torch.Tensor,
+                        indices: torch.Tensor):
+    """``normed * (1 + scale[indices]) + shift[indices]`` (bf16 rounding after
+    each op, as the stock expression), or MISS."""
+    from h3_engine_b200 import ops
+    if not _gather_covered(normed, (scale, shift), indices):
+        return MISS
+    return ops.ada_modulate(normed, scale, shift, indices)
+
+
+def gate_residual_kernel(residual: torch.Tensor, y: torch.Tensor, gate: torch.Tensor,
+                         indices: torch.Tensor):
+    """``residual + gate[indices] * y`` (bf16 rounding after each op), or MISS."""
+    from h3_engine_b200 import ops
+    if not (isinstance(y, torch.Tensor) and isinstance(residual, torch.Tensor)):
+        return MISS
+    if y.shape != residual.shape or not (y.is_cuda and y.dtype == torch.bfloat16):
+        return MISS
+    if not _gather_covered(residual, (gate,), indices):
+        return MISS
+    return ops.gate_residual(residual, y, gate, indices)
+
+
 def ada_modulate(normed: torch.Tensor, scale: torch.Tensor, shift: torch.Tensor,
                  indices: torch.Tensor) -> torch.Tensor:
     """``normed * (1 + scale[indices]) + shift[indices]``."""
+    if enabled("H3_FUSED_MODULATE"):
+        out = ada_modulate_kernel(normed, scale, shift, indices)
+        if out is not MISS:
+            return out
+        note_miss("ada_modulate_gather")
     return normed * (1.0 + scale.index_select(0, indices)) + shift.index_select(0, indices)
 
 
@@ -168,4 +247,9 @@ def norm_rope(norm_module: nn.RMSNorm, x: torch.Tensor, cos: torch.Tensor,
 def gate_residual(residual: torch.Tensor, y: torch.Tensor, gate: torch.Tensor,
                   indices: torch.Tensor) -> torch.Tensor:
     """``residual + gate[indices] * y``."""
+    if enabled("H3_FUSED_GATE"):
+        out = gate_residual_kernel(residual, y, gate, indices)
+        if out is not MISS:
+            return out
+        note_miss("gate_residual_gather")
     return _gate_residual_impl(residual, y, gate, indices)

@@ -265,3 +265,103 @@ def attention_varlen(qkv: torch.Tensor, heads: int, head_dim: int, cu_seqlens, *
     _H3B.attention_varlen(q2, rows, q2.stride(0), q_off, q_row0, kv2, kv2.shape[0], kv2.stride(0),
                           k_off, v_off, heads, head_dim, cu, sc, out)
     return out
+
+
+def _rows2d(t: torch.Tensor) -> torch.Tensor:
+    """A [rows, C] view with a contiguous last dim and 8-element row stride
+    (a copy only when the layout needs one)."""
+    t2 = t.reshape(-1, t.shape[-1]) if t.dim() != 2 else t
+    if t2.stride(-1) != 1 or t2.stride(0) % 8 or t2.storage_offset() % 8:
+        t2 = t2.contiguous()
+    return t2
+
+
+def qk_norm_rope_out(x: torch.Tensor, heads: int, head_dim: int, *, w: torch.Tensor | None,
+                     eps: float, cos: torch.Tensor | None, sin: torch.Tensor | None,
+                     out: torch.Tensor | None = None) -> torch.Tensor:
+    """Per-head RMSNorm (``w``) + rotate-half RoPE of ``x`` [rows, heads*head_dim]
+    (any row stride) into a new contiguous ``out``; ``x`` is left untouched.
+    ``cos``/``sin``: fp32 [rows, R]."""
+    dev = _need_cuda(x, w, cos, sin, out)
+    x2 = _rows2d(x)
+    if x2.dtype != torch.bfloat16 or x2.shape[1] != heads * head_dim:
+        raise ValueError("x must be bf16 [rows, heads * head_dim]")
+    T = x2.shape[0]
+    if out is None:
+        out = torch.empty(T, heads * head_dim, dtype=torch.bfloat16, device=dev)
+    R, cs = 0, 0
+    if cos is not None:
+        cos, sin = cos.reshape(T, -1), sin.reshape(T, -1)
+        if cos.dtype != torch.float32 or sin.dtype != torch.float32:
+            cos, sin = cos.float(), sin.float()
+        if (cos.stride(-1) != 1 or sin.stride(-1) != 1 or cos.stride(0) != sin.stride(0)
+                or cos.stride(0) % 4 or cos.storage_offset() % 4 or sin.storage_offset() % 4):
+            cos, sin = cos.contiguous(), sin.contiguous()
+        R, cs = cos.shape[1], cos.stride(0)
+    _H3B.qk_norm_rope_out(x2, x2.stride(0), None, 0, out, out.stride(0), None, 0, T, heads,
+                          head_dim, w, None, float(eps), cos, sin, R, cs)
+    return out
+
+
+def attention_qkv(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, heads: int, head_dim: int,
+                  cu_seqlens, *, scale: float | None = None,
+                  out: torch.Tensor | None = None) -> torch.Tensor:
+    """Attention per document over separate q, k, v activations
+    [rows, heads*head_dim] (any row strides): no concatenation of k and v."""
+    dev = _need_cuda(q, k, v, out)
+    q2, k2, v2 = _rows2d(q), _rows2d(k), _rows2d(v)
+    for t in (q2, k2, v2):
+        if t.dtype != torch.bfloat16 or t.shape != q2.shape:
+            raise ValueError("q, k, v must be bf16 [rows, heads * head_dim] of one shape")
+    rows = q2.shape[0]
+    cu = [int(c) for c in (cu_seqlens.tolist() if hasattr(cu_seqlens, "tolist") else cu_seqlens)]
+    if out is None:
+        out = torch.empty(rows, heads * head_dim, dtype=torch.bfloat16, device=dev)
+    sc = float(scale) if scale is not None else head_dim ** -0.5
+    _H3B.attention_qkv(q2, q2.stride(0), k2, k2.stride(0), v2, v2.stride(0), rows, heads,
+                       head_dim, cu, sc, out)
+    return out
+
+
+def _table_rows(idx: torch.Tensor | None, dev) -> tuple[torch.Tensor | None, int]:
+    if idx is None:
+        return None, 0
+    if idx.dtype != torch.int32 or not idx.is_contiguous():
+        idx = idx.to(torch.int32).contiguous()
+    return idx, idx.numel()
+
+
+def gate_residual(residual: torch.Tensor, y: torch.Tensor, gate: torch.Tensor,
+                  idx: torch.Tensor | None, out: torch.Tensor | None = None) -> torch.Tensor:
+    """``residual + gate[idx] * y`` with torch's bf16 rounding after each op;
+    ``residual``/``y`` [..., C] bf16, ``gate`` bf16 [n, C], ``idx`` per row,
+    repeating over leading dims (row r uses ``idx[r % len(idx)]``)."""
+    dev = _need_cuda(residual, y, gate, idx, out)
+    r2, y2 = _rows2d(residual), _rows2d(y)
+    g2 = gate.reshape(-1, gate.shape[-1]).contiguous()
+    rows, C = r2.shape
+    if y2.shape != r2.shape or g2.shape[1] != C:
+        raise ValueError("residual, y and gate must agree on [rows, C]")
+    i2, n = _table_rows(idx, dev)
+    if out is None:
+        out = torch.empty(residual.shape, dtype=torch.bfloat16, device=dev)
+    o2 = out.view(rows, C)
+    _H3B.gate_residual(r2, r2.stride(0), y2, y2.stride(0), g2, i2, n, rows, C, o2, o2.stride(0))
+    return out
+
+
+def ada_modulate(x: torch.Tensor, scale: torch.Tensor, shift: torch.Tensor,
+                 idx: torch.Tensor | None, out: torch.Tensor | None = None) -> torch.Tensor:
+    """``x * (1 + scale[idx]) + shift[idx]`` with torch's bf16 rounding after
+    each op (tables bf16 [n, C], row r uses ``idx[r % len(idx)]``)."""
+    dev = _need_cuda(x, scale, shift, idx, out)
+    x2 = _rows2d(x)
+    rows, C = x2.shape
+    sc = scale.reshape(-1, C).contiguous()
+    sh = shift.reshape(-1, C).contiguous()
+    i2, n = _table_rows(idx, dev)
+    if out is None:
+        out = torch.empty(x.shape, dtype=torch.bfloat16, device=dev)
+    o2 = out.view(rows, C)
+    _H3B.ada_modulate(x2, x2.stride(0), sc, sh, i2, n, rows, C, o2, o2.stride(0))
+    return out

@@ -135,3 +135,46 @@ def attention_varlen(q_buf: torch.Tensor, q_rows: int, q_stride: int, q_off: int
     _run(out, "h3b_attention_varlen", _p(q_buf), q_rows, q_stride, q_off, q_row0, _p(kv_buf),
          kv_rows, kv_stride, k_off, v_off, heads, head_dim, arr, len(cu_seqlens) - 1,
          float(scale), _p(out), out.stride(0))
+
+
+@_op("qk_norm_rope_out", ("q_out", "k_out"))
+def qk_norm_rope_out(q: Optional[torch.Tensor], q_stride: int, k: Optional[torch.Tensor],
+                     k_stride: int, q_out: Optional[torch.Tensor], qo_stride: int,
+                     k_out: Optional[torch.Tensor], ko_stride: int, rows: int, heads: int,
+                     head_dim: int, wq: Optional[torch.Tensor], wk: Optional[torch.Tensor],
+                     eps: float, cos: Optional[torch.Tensor], sin: Optional[torch.Tensor],
+                     rot: int, cs_stride: int) -> None:
+    """Per-head RMSNorm + RoPE from q / k into q_out / k_out (h3b_qk_norm_rope_out)."""
+    ref = q_out if q_out is not None else k_out
+    _run(ref, "h3b_qk_norm_rope_out", _p(q), q_stride, _p(k), k_stride, _p(q_out), qo_stride,
+         _p(k_out), ko_stride, rows, heads, head_dim, _p(wq), _p(wk), float(eps), _p(cos),
+         _p(sin), rot, cs_stride)
+
+
+@_op("attention_qkv", ("out",))
+def attention_qkv(q: torch.Tensor, q_stride: int, k: torch.Tensor, k_stride: int,
+                  v: torch.Tensor, v_stride: int, rows: int, heads: int, head_dim: int,
+                  cu_seqlens: list[int], scale: float, out: torch.Tensor) -> None:
+    """Packed varlen attention over separate q, k, v rows (h3b_attention_qkv)."""
+    import ctypes
+    arr = (ctypes.c_int32 * len(cu_seqlens))(*cu_seqlens)
+    _run(out, "h3b_attention_qkv", _p(q), q_stride, _p(k), k_stride, _p(v), v_stride, rows,
+         heads, head_dim, arr, len(cu_seqlens) - 1, float(scale), _p(out), out.stride(0))
+
+
+@_op("gate_residual", ("out",))
+def gate_residual(residual: torch.Tensor, ldr: int, y: torch.Tensor, ldy: int,
+                  gate: torch.Tensor, idx: Optional[torch.Tensor], n_idx: int, rows: int,
+                  cols: int, out: torch.Tensor, ldo: int) -> None:
+    """out = residual + gate[idx] * y, torch's bf16 rounding (h3b_gate_residual)."""
+    _run(out, "h3b_gate_residual", _p(residual), ldr, _p(y), ldy, _p(gate), _p(idx), n_idx, rows,
+         cols, _p(out), ldo)
+
+
+@_op("ada_modulate", ("out",))
+def ada_modulate(x: torch.Tensor, ldx: int, scale: torch.Tensor, shift: torch.Tensor,
+                 idx: Optional[torch.Tensor], n_idx: int, rows: int, cols: int,
+                 out: torch.Tensor, ldo: int) -> None:
+    """out = x * (1 + scale[idx]) + shift[idx], torch's bf16 rounding (h3b_ada_modulate)."""
+    _run(out, "h3b_ada_modulate", _p(x), ldx, _p(scale), _p(shift), _p(idx), n_idx, rows, cols,
+         _p(out), ldo)

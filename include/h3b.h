@@ -162,6 +162,36 @@ H3B_API int h3b_qk_norm_rope(void* q, int64_t q_stride, int64_t q_off, void* k, 
                              const void* wk, float eps, const float* cos, const float* sin, int R,
                              int64_t cs_stride, void* stream);
 
+/* The same, out of place: query heads read from q (head h at column h*D of
+ * row t, row stride q_stride) and written to q_out (row stride qo_stride),
+ * key heads from k to k_out likewise; q or k may be NULL (with its output),
+ * not both.  The function form of the row shims norm_rope / apply_rotary_emb
+ * (h3_inference/kernels/elementwise_norm_rope.py:25-40,133-148), whose
+ * inputs stay untouched.  Limits as above.                                */
+H3B_API int h3b_qk_norm_rope_out(const void* q, int64_t q_stride, const void* k, int64_t k_stride,
+                                 void* q_out, int64_t qo_stride, void* k_out, int64_t ko_stride,
+                                 int64_t T, int H, int D, const void* wq, const void* wk, float eps,
+                                 const float* cos, const float* sin, int R, int64_t cs_stride,
+                                 void* stream);
+
+/* ------------------------------------------------------------------ gathered adaLN ops
+ * Per-row table gathers of the reference block, bf16 [rows, cols] (row
+ * strides in elements, cols % 8 == 0, 16-byte aligned rows), the table row
+ * of row r being idx[r % n_idx] (idx NULL: row 0), with torch's bf16 rounding
+ * after every op (bit-identical to the reference's stock expressions):
+ *   h3b_gate_residual: out = residual + gate[idx] * y
+ *     (gate_residual, h3_inference/kernels/elementwise_norm_rope.py:150-163)
+ *   h3b_ada_modulate:  out = x * (1 + scale[idx]) + shift[idx]
+ *     (ada_modulate, h3_inference/kernels/elementwise_norm_rope.py:90-102)
+ * Tables are bf16 [n_rows, cols]; every idx value must be >= 0 and below
+ * n_rows (not checked).  out may alias residual / x (same strides).        */
+H3B_API int h3b_gate_residual(const void* residual, int64_t ldr, const void* y, int64_t ldy,
+                              const void* gate, const int32_t* idx, int64_t n_idx, int64_t rows,
+                              int64_t cols, void* out, int64_t ldo, void* stream);
+H3B_API int h3b_ada_modulate(const void* x, int64_t ldx, const void* scale, const void* shift,
+                             const int32_t* idx, int64_t n_idx, int64_t rows, int64_t cols,
+                             void* out, int64_t ldo, void* stream);
+
 /* ------------------------------------------------------------------ packed varlen attention
  * out[i, h*D + d] = softmax_j(q_i . k_j * scale) v_j for every local query row
  * i, over the keys j of the document that contains its global row q_row0 + i
@@ -182,6 +212,17 @@ H3B_API int h3b_attention_varlen(const void* q_buf, int64_t q_rows, int64_t q_st
                                  int64_t kv_stride, int64_t k_off, int64_t v_off, int H, int D,
                                  const int32_t* cu_seqlens_host, int ndocs, float scale,
                                  void* out, int64_t ldo, void* stream);
+
+/* The same attention over three separate bf16 activations [rows, *]: head h
+ * of q, k and v at column h*D of their rows (row strides q_stride, k_stride,
+ * v_stride), every row a query and a key; the shape of
+ * packed_self_attention's (B, T, H, D) query / key / value tensors
+ * (h3_inference/kernels/packed_self_attn.py:8-37), which need not share a
+ * buffer.  Limits as above.                                                 */
+H3B_API int h3b_attention_qkv(const void* q, int64_t q_stride, const void* k, int64_t k_stride,
+                              const void* v, int64_t v_stride, int64_t rows, int H, int D,
+                              const int32_t* cu_seqlens_host, int ndocs, float scale, void* out,
+                              int64_t ldo, void* stream);
 
 /* ------------------------------------------------------------------ no-allocation variant
  * No counterpart in the reference.  The same RMSNorm(+modulation) -> NVFP4

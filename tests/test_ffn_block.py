@@ -198,3 +198,31 @@ def test_ffn_block_full_size_row_sample(cuda):
     y_r, _ = B.nvfp4_linear_from_bf16(u_r, *oracle_weights(w2), bias=b2.float().numpy(),
                                       residual=xs, gs_a=gs_u)
     assert R.max_rel_err(y[rows.to(cuda)].float().cpu().numpy(), y_r) <= TOL
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("M,K", [(1000, 3072), (300, 5376), (129, 5888)])
+def test_rmsnorm_modulated_cfg_halves(cuda, M, K):
+    """Modulation rows in contiguous halves (the stacked CFG pair): CTAs whose
+    rows share one modulation row use the shared-memory table path, the CTA
+    at the boundary (and K beyond the table limit) the per-element path; y
+    within 1e-2 of the oracle and the packed bytes bit-exact against the
+    oracle quantizer applied to the GPU's y."""
+    from h3_engine_b200 import ops
+    g = torch.Generator().manual_seed(M + 7 * K)
+    x = torch.randn(M, K, generator=g).to(torch.bfloat16)
+    gamma = (1 + 0.1 * torch.randn(K, generator=g)).to(torch.bfloat16)
+    shift = (0.1 * torch.randn(2, K, generator=g)).to(torch.bfloat16)
+    scale = (0.1 * torch.randn(2, K, generator=g)).to(torch.bfloat16)
+    idx = (torch.arange(M) >= M // 2 + 3).to(torch.int32)      # boundary inside a CTA
+    q, sf, gs, y = ops.rmsnorm_quantize(x.to(cuda), gamma.to(cuda), 1e-6, shift=shift.to(cuda),
+                                        scale=scale.to(cuda), mod_idx=idx.to(cuda), return_y=True)
+    torch.cuda.synchronize()
+    yg = y.float().cpu().numpy()
+    yr = B.rmsnorm(x.float().numpy(), gamma.float().numpy(), 1e-6, shift.float().numpy(),
+                   scale.float().numpy(), idx.numpy())
+    assert R.max_rel_err(yg, yr) <= 1e-2
+    assert gs.item() == float(np.float32(np.abs(yg).max()) / np.float32(2688.0))
+    rq, rs, _ = R.quantize(yg, mpad=q.shape[0])
+    assert np.array_equal(q.cpu().numpy(), rq)
+    assert np.array_equal(sf.cpu().numpy(), R.swizzle(rs))

@@ -39,12 +39,16 @@ def test_dispatch_surface(flags):
     assert D.enabled("H3_FUSED_ROPE") and D.enabled("H3_NVFP4")
     assert D.armed_counts(reset=True) == {"H3_FUSED_ROPE": 1, "H3_NVFP4": 1}
     D.miss_counts(reset=True)
-    # names with no kernel here, and arguments the kernels do not take (CPU tensors)
+    # a name with no kernel, and arguments the kernels do not take (not
+    # tensors, CPU tensors)
+    assert D.try_call("no_such_row", 1) is D.MISS
     assert D.try_call("gate_residual_gather", 1, 2, 3, 4) is D.MISS
     x = torch.zeros(1, 8, 2, 128, dtype=torch.bfloat16)
     cs = torch.zeros(8, 128)
     assert D.try_call("rope", x, cs, cs) is D.MISS
-    assert D.miss_counts() == {"gate_residual_gather": 1, "rope": 1}
+    assert D.try_call("ada_modulate_gather", x, cs, cs, torch.zeros(8, dtype=torch.long)) is D.MISS
+    assert D.miss_counts() == {"no_such_row": 1, "gate_residual_gather": 1, "rope": 1,
+                               "ada_modulate_gather": 1}
 
 
 def test_flags_off_paths_are_the_stock_expressions(flags):
@@ -183,7 +187,126 @@ def test_attention_shim_matches_sdpa(cuda, flags, B, T, H):
                               v.reshape(B, T, -1), H)
     assert torch.equal(flat.view(B, T, H, 128), out)
     mask = torch.ones(T, T, dtype=torch.bool, device=cuda)
-    assert rel(at.packed_self_attention(q, k, v, mask), ref) <= 1e-2   # masked: SDPA path
+    assert rel(at.packed_self_attention(q, k, v, mask), ref) <= 1e-2   # one document
+    # key / value views of one projection output (row stride 3*H*D): read in place
+    qkv = torch.cat([q.flatten(2), k.flatten(2), v.flatten(2)], dim=-1)
+    qv, kv, vv = (qkv[..., i * H * 128:(i + 1) * H * 128].unflatten(-1, (H, 128)) for i in range(3))
+    assert torch.equal(at.packed_self_attention(qv, kv, vv), out)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("B,T,H", [(1, 400, 2), (2, 300, 3)])
+def test_attention_shim_pad_mask_as_documents(cuda, flags, B, T, H):
+    """The reference model's pad mask (is_pad[None, :] == is_pad[:, None],
+    h3_inference/transformer/model.py:326-329) runs on the kernel as two
+    documents of a permuted sequence; SDPA with the same mask is the bar."""
+    from h3_engine_b200.kernels import _dispatch
+    from h3_engine_b200.kernels import packed_self_attn as at
+    g = torch.Generator().manual_seed(T + H)
+    q, k, v = (torch.randn(B, T, H, 128, generator=g).to(torch.bfloat16).to(cuda)
+               for _ in range(3))
+    is_pad = torch.rand(T, generator=g) < 0.3
+    mask = (is_pad[None, :] == is_pad[:, None]).to(cuda)
+    causal = torch.tril(torch.ones(T, T, dtype=torch.bool, device=cuda))
+    ref = at.packed_self_attention(q, k, v, mask)                    # flag off: SDPA
+    ref_causal = at.packed_self_attention(q, k, v, causal)
+    flags("H3_TL_ATTN")
+    _dispatch.miss_counts(reset=True)
+    out = at.packed_self_attention(q, k, v, mask)
+    assert _dispatch.miss_counts() == {}
+    assert rel(out, ref) <= 1e-2
+    # a mask of another form stays on SDPA (counted as a miss)
+    out2 = at.packed_self_attention(q, k, v, causal)
+    assert _dispatch.miss_counts() == {"attention": 1}
+    assert torch.equal(out2, ref_causal)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("B,T,C,n", [(1, 300, 512, 3), (2, 129, 1024, 6)])
+def test_gate_residual_and_ada_modulate_shims_bit_exact(cuda, flags, B, T, C, n):
+    """The gathered gate + residual and modulation kernels give the stock
+    bf16 expressions' bytes (torch rounds after every op; so do they)."""
+    from h3_engine_b200.kernels import _dispatch
+    from h3_engine_b200.kernels import elementwise_norm_rope as ew
+    g = torch.Generator().manual_seed(C + n)
+    x, y = (torch.randn(B, T, C, generator=g).to(torch.bfloat16).to(cuda) for _ in range(2))
+    gate, scale, shift = ((0.3 * torch.randn(n, C, generator=g)).to(torch.bfloat16).to(cuda)
+                          for _ in range(3))
+    idx = torch.randint(0, n, (T,), generator=g).to(cuda)
+    ref_g = ew.gate_residual(x, y, gate, idx)                        # flags off: stock
+    ref_m = ew.ada_modulate(x, scale, shift, idx)
+    flags("H3_FUSED_GATE", "H3_FUSED_MODULATE")
+    _dispatch.miss_counts(reset=True)
+    assert torch.equal(ew.gate_residual(x, y, gate, idx), ref_g)
+    assert torch.equal(ew.ada_modulate(x, scale, shift, idx), ref_m)
+    assert _dispatch.miss_counts() == {}
+    assert torch.equal(_dispatch.try_call("gate_residual_gather", x, y, gate, idx), ref_g)
+    assert torch.equal(_dispatch.try_call("ada_modulate_gather", x, scale, shift, idx), ref_m)
+
+
+@pytest.mark.gpu
+def test_rope_shim_is_out_of_place(cuda, flags):
+    """norm_rope returns a new tensor and leaves its (strided) input as it was."""
+    from h3_engine_b200.kernels import elementwise_norm_rope as ew
+    g = torch.Generator().manual_seed(12)
+    T, H = 257, 3
+    qkv = torch.randn(1, T, 3 * H * 128, generator=g).to(torch.bfloat16).to(cuda)
+    q = qkv[..., :H * 128].unflatten(-1, (H, 128))                  # a strided view
+    norm = nn.RMSNorm(128, eps=1e-5).to(cuda).to(torch.bfloat16)
+    with torch.no_grad():
+        norm.weight.copy_(1 + 0.1 * torch.randn(128, generator=g))
+    ang = torch.rand(T, 48, generator=g).to(cuda) * 6.28
+    cos = torch.cat([ang.cos(), ang.cos()], 1)
+    sin = torch.cat([ang.sin(), ang.sin()], 1)
+    before = qkv.clone()
+    ref = ew._norm_rope_impl(q, norm.weight, 1e-5, cos, sin)
+    flags("H3_FUSED_ROPE")
+    out = ew.norm_rope(norm, q, cos, sin)
+    assert torch.equal(qkv, before)
+    assert out.shape == q.shape and out.is_contiguous()
+    assert rel(out, ref) <= 1e-2
+
+
+@pytest.mark.gpu
+def test_shims_take_reference_style_quantized_linears(cuda, flags):
+    """Modules carrying the reference's own NVFP4 weight object (slots qdata_t
+    and scale, no global scale: its two-level scheme) reach the kernels
+    through shared_qkv / out_projection: global scale 1 on the GEMM."""
+    from h3_engine_b200 import nvfp4, ops
+    from h3_engine_b200.kernels import _dispatch
+    from h3_engine_b200.kernels import ffn_qkvo_gemms as gm
+
+    class _RefWeight:                         # the reference NVFP4Weight's slots
+        __slots__ = ("qdata_t", "scale", "in_features", "out_features", "dtype")
+
+    class _RefQuantLinear(nn.Module):         # the reference _QuantLinear's attributes
+        def __init__(self, w):
+            super().__init__()
+            q, sf, _ = ops.quantize(w, mpad=w.shape[0], gs=1.0)
+            rw = _RefWeight()
+            rw.qdata_t = q.view(torch.float4_e2m1fn_x2).t()
+            rw.scale = sf.view(torch.float8_e4m3fn)
+            rw.out_features, rw.in_features = w.shape
+            rw.dtype = torch.bfloat16
+            self.weight_nvfp4 = rw
+            self.in_features, self.out_features, self.calls = w.shape[1], w.shape[0], 0
+
+    g = torch.Generator().manual_seed(13)
+    T, d = 200, 512
+    x = torch.randn(1, T, d, generator=g).to(torch.bfloat16).to(cuda)
+    ws = [(0.05 * torch.randn(d, d, generator=g)).to(torch.bfloat16).to(cuda) for _ in range(4)]
+    mods = [_RefQuantLinear(w) for w in ws]
+    flags("H3_NVFP4")
+    _dispatch.miss_counts(reset=True)
+    q, k, v = gm.qkv_projection(mods[0], mods[1], mods[2], x)
+    o = gm.out_projection(mods[3], x)
+    assert _dispatch.miss_counts() == {}
+    assert [m.calls for m in mods] == [1, 1, 1, 1]
+    # the same GEMMs through this library's own weight objects at global scale 1
+    for got, w in zip((q, k, v, o), ws):
+        qw, sw, _ = ops.quantize(w, mpad=d, gs=1.0)
+        mine = nvfp4.NVFP4Weight.from_packed(qw, sw, d, d, 1.0)
+        assert torch.equal(got, nvfp4.QuantizedActivation(x).mm(mine))
 
 
 class _SwiGLU(nn.Module):

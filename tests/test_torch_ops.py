@@ -22,6 +22,10 @@ OPS = {
     "rmsnorm_quantize": {"gs_out", "q", "sf", "y_out"},
     "qk_norm_rope": {"buf", "k_buf"},
     "attention_varlen": {"out"},
+    "qk_norm_rope_out": {"q_out", "k_out"},
+    "attention_qkv": {"out"},
+    "gate_residual": {"out"},
+    "ada_modulate": {"out"},
 }
 
 
