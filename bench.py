@@ -405,6 +405,130 @@ class RefBlockWorkload:
         self.y_h.copy_(self.y, non_blocking=True)
 
 
+class RefShimsWorkload:
+    """The same reference-shape block, built as a module tree with the
+    reference's module names (norm1, attn.{to_q,to_k,to_v,norm_q,norm_k,
+    to_out.0}, norm2, ff.net.{0.proj,2}), its six linears swapped by
+    ``nvfp4.quantize_blocks``, and run through the row shims of
+    ``h3_engine_b200.kernels`` in the order H3TransformerBlock.forward calls
+    them (h3_inference/transformer/model.py:81-106,176-209) with H3_KERNELS=1:
+    the reference-API (drop-in) path, every row on a kernel."""
+    name = "refblock-shims"
+    C, H, D, F, TOKENS = RefBlockWorkload.C, RefBlockWorkload.H, RefBlockWorkload.D, \
+        RefBlockWorkload.F, RefBlockWorkload.TOKENS
+
+    def __init__(self, dev, world: int, rank: int):
+        from torch import nn
+
+        from h3_engine_b200 import nvfp4
+        from h3_engine_b200.rope import reference_dims, rope_tables
+        os.environ["H3_KERNELS"] = "1"
+        C, H, D, F, T = self.C, self.H, self.D, self.F, self.TOKENS
+        HD = H * D
+        g = torch.Generator(device=dev).manual_seed(5 + 1000 * rank)
+
+        def lin(n, k):
+            m = nn.Linear(k, n, bias=False, device=dev, dtype=torch.bfloat16)
+            with torch.no_grad():
+                m.weight.copy_(torch.randn(n, k, generator=g, device=dev) / k ** 0.5)
+            return m
+
+        def rms(n):
+            m = nn.RMSNorm(n, eps=1e-5, device=dev, dtype=torch.bfloat16)
+            with torch.no_grad():
+                m.weight.copy_(1 + 0.1 * torch.randn(n, generator=g, device=dev))
+            return m
+
+        blk = nn.Module()
+        blk.norm1, blk.norm2 = rms(C), rms(C)
+        blk.attn = nn.Module()
+        blk.attn.heads = H
+        blk.attn.to_q, blk.attn.to_k, blk.attn.to_v = lin(HD, C), lin(HD, C), lin(HD, C)
+        blk.attn.norm_q, blk.attn.norm_k = rms(D), rms(D)
+        blk.attn.to_out = nn.ModuleList([lin(C, HD), nn.Dropout(0.0)])
+        up = nn.Module()
+        up.proj, up.activation = lin(2 * F, C), nn.SiLU()
+        blk.ff = nn.Module()
+        blk.ff.net = nn.ModuleList([up, nn.Dropout(0.0), lin(C, F)])
+        model = nn.Module()
+        model.transformer_blocks = nn.ModuleList([blk])
+        nvfp4.quantize_blocks(model, self_check=False)
+        self.blk = blk
+        self.tables = tuple(((0.5 if j in (2, 5) else 0.0)
+                             + 0.1 * torch.randn(3, C, generator=g, device=dev)).to(torch.bfloat16)
+                            for j in range(6))
+        n_vid = T - 2048
+        self.idx = torch.cat([torch.zeros(n_vid), torch.ones(1024), 2 * torch.ones(1024)]).to(
+            torch.long).to(dev)
+        pos = torch.stack([torch.arange(T) // 1024, (torch.arange(T) // 32) % 32,
+                           torch.arange(T) % 32], dim=1).float().to(dev)
+        self.rope = rope_tables(pos, reference_dims(16), 10000.0)
+        self.x = torch.randn(1, T, C, generator=g, device=dev).to(torch.bfloat16)
+        self.rank_gemm_flops = RefBlockWorkload.gemm_flops()
+        self.rank_attn_flops = 4 * HD * T * T
+        self.step_flops = world * (self.rank_gemm_flops + self.rank_attn_flops)
+        self.attn_traffic = T * (3 * HD * 2 + HD * 2)
+        self.attn_events = None
+        self.config = self.describe(world)
+
+    @classmethod
+    def describe(cls, world: int) -> dict:
+        d = RefBlockWorkload.describe(world)
+        d["workload"] = ("one H3TransformerBlock at the reference model's shapes through the "
+                         "reference-API row shims (norm_modulate, qkv_projection, norm_rope, "
+                         "packed_self_attention, out_projection, gate_residual, ffn) with "
+                         "H3_KERNELS=1")
+        return d
+
+    def set_timers(self, gemm, attn):
+        self.attn_events = attn
+
+    def _forward(self, x):
+        from h3_engine_b200 import ops
+        from h3_engine_b200.kernels import elementwise_norm_rope as ew
+        from h3_engine_b200.kernels import ffn_qkvo_gemms as gm
+        from h3_engine_b200.kernels import packed_self_attn as at
+        blk, idx, cos_sin = self.blk, self.idx, self.rope
+        shift_a, scale_a, gate_a, shift_m, scale_m, gate_m = self.tables
+        h = ew.norm_modulate(blk.norm1, x, scale_a, shift_a, idx)
+        a = blk.attn
+        q, k, v = gm.qkv_projection(a.to_q, a.to_k, a.to_v, h)
+        q, k, v = (t.unflatten(-1, (a.heads, -1)) for t in (q, k, v))
+        q = ew.norm_rope(a.norm_q, q, *cos_sin)
+        k = ew.norm_rope(a.norm_k, k, *cos_sin)
+        ev = self.attn_events
+        if ev is not None:
+            e0 = torch.cuda.Event(enable_timing=True)
+            e0.record()
+        o = at.packed_self_attention(q, k, v, None)
+        if ev is not None:
+            e1 = torch.cuda.Event(enable_timing=True)
+            e1.record()
+            ev.append((e0, e1))
+        o = gm.out_projection(a.to_out[0], o.flatten(2, 3).type_as(q))
+        x = ew.gate_residual(x, o, gate_a, idx)
+        h = ew.norm_modulate(blk.norm2, x, scale_m, shift_m, idx)
+        return ew.gate_residual(x, gm.ffn(blk.ff, h), gate_m, idx)
+
+    def step(self):
+        from h3_engine_b200.kernels import _dispatch
+        _dispatch.miss_counts(reset=True)
+        self.y = self._forward(self.x)
+        if _dispatch.miss_counts():
+            raise RuntimeError(f"a row shim fell back to torch: {_dispatch.miss_counts()}")
+
+    def e2e_setup(self):
+        self.x_h = self.x.cpu().pin_memory()
+        self.y_h = torch.empty_like(self.x_h).pin_memory()
+        self.x_d = torch.empty_like(self.x)
+        return self.x_h.numel() * 2, self.y_h.numel() * 2
+
+    def e2e_step(self):
+        self.x_d.copy_(self.x_h, non_blocking=True)
+        y = self._forward(self.x_d)
+        self.y_h.copy_(y, non_blocking=True)
+
+
 class QuantWorkload:
     """The quantize / pack microbenchmark: amax + NVFP4 quantization (codes,
     blocked e4m3 scales, fp32 global scale) of bf16 [M, K] for M in {4096,
@@ -460,6 +584,29 @@ class QuantWorkload:
 
     def step(self):
         self._run(self.xs)
+
+    def unpack_rate(self, pk, reps: int = 10) -> dict:
+        """The unpack of config 1 (codes + block scales + global scale ->
+        bf16, 2.5625 B per element), CUDA events over ``reps`` passes of the
+        four shapes after the timed region."""
+        ops = self.ops
+        outs = [torch.empty_like(x) for x in self.xs]
+
+        def run():
+            for x, (q, sf, _, gs), o in zip(self.xs, self.outs, outs):
+                ops.dequantize(q, sf, gs, x.shape[0], x.shape[1], out=o)
+        run()
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(reps):
+            run()
+        b.record()
+        torch.cuda.synchronize()
+        ms = a.elapsed_time(b) / reps
+        gbs = 2.5625 * sum(x.numel() for x in self.xs) / (ms * 1e-3) / 1e9
+        return {"kernel": "h3b::k_nvfp4_dequantize<swizzled>", "ms_per_pass": ms,
+                "achieved": gbs, "unit": "GB/s", "frac": gbs / pk["hbm"]}
 
     def roofline(self, pk, steps, ms, kernel_ms):
         achieved = self.quant_bytes * steps / (kernel_ms * 1e-3) / 1e9
@@ -648,7 +795,7 @@ def cpu_baseline_run(args) -> dict | None:
     if args.workload == "attention":
         return cpu_attention_run([int(n) for n in args.attn_docs.split(",")], args.cpu_rows,
                                  args.cpu_seconds)
-    if args.workload == "refblock":
+    if args.workload in ("refblock", "refblock-shims"):
         return cpu_refblock_run(args.cpu_rows, args.cpu_seconds)
     return None
 
@@ -666,14 +813,17 @@ def run_reference(args) -> None:
                "quant": lambda: QuantWorkload.describe(args.gpus),
                "attention": lambda: AttentionWorkload.describe(
                    args.gpus, [int(n) for n in args.attn_docs.split(",")]),
-               "refblock": lambda: RefBlockWorkload.describe(args.gpus)}
+               "refblock": lambda: RefBlockWorkload.describe(args.gpus),
+               "refblock-shims": lambda: RefShimsWorkload.describe(args.gpus)}
     dtypes = {"dit": "fp32 (NVFP4 operands decoded)", "ffn": "fp32 (NVFP4 operands decoded)",
               "quant": "fp32 -> e2m1 / e4m3", "attention": "fp32 (bf16 q|k|v)",
-              "refblock": "fp32 (NVFP4 operands decoded)"}
+              "refblock": "fp32 (NVFP4 operands decoded)",
+              "refblock-shims": "fp32 (NVFP4 operands decoded)"}
     line = {
         "impl": "reference", "metric": METRIC, "value": v, "unit": unit,
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": statistics.median([x["s_per_step"] for x in vals]) * 1e3,
+        "ms_per_step_is": "extrapolated: the timed CPU sample scaled linearly to the whole step",
         "higher_is_better": True, "scaling": "strong" if args.workload == "dit" else "weak",
         "vs_baseline": None, "dtype": dtypes[args.workload],
         "data": "synthetic",
@@ -706,6 +856,8 @@ def run_ours(args) -> None:
         wl = FFNWorkload(dev, world, rank)
     elif args.workload == "refblock":
         wl = RefBlockWorkload(dev, world, rank)
+    elif args.workload == "refblock-shims":
+        wl = RefShimsWorkload(dev, world, rank)
     elif args.workload == "quant":
         wl = QuantWorkload(dev, world, rank)
     else:
@@ -780,6 +932,8 @@ def run_ours(args) -> None:
         gemm_tflops = wl.rank_gemm_flops / (gemm_ms * 1e-3) / 1e12 if gemm_ms else None
         if hasattr(wl, "roofline"):
             roof = wl.roofline(pk, args.steps, ms, sum(attn_list))
+            if hasattr(wl, "unpack_rate"):
+                extras["unpack"] = wl.unpack_rate(pk)
         elif attn_list:
             n_launch = len(attn_list)
             flops_launch = wl.rank_attn_flops * args.steps / n_launch
@@ -788,7 +942,7 @@ def run_ours(args) -> None:
             roof = {"bound": "tensor", "kernel": "h3b::attn::k_fmha (bf16)", "achieved": achieved,
                     "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
                     "peak_source": f"bf16_tflops_sustained of {pk['source']} MEASURED_PEAKS.json",
-                    "traffic": (wl.attn_traffic if wl.name in ("dit", "refblock")
+                    "traffic": (wl.attn_traffic if wl.name in ("dit", "refblock", "refblock-shims")
                                 else ATTN_TRAFFIC_PER_TOKEN * wl.cu[-1]),
                     "per_launch_tflop": flops_launch / 1e12,
                     "launch_ms": statistics.mean(attn_list),
@@ -965,7 +1119,8 @@ def main() -> None:
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["h3b", "reference"], default="h3b")
-    ap.add_argument("--workload", choices=["dit", "ffn", "attention", "refblock", "quant"],
+    ap.add_argument("--workload", choices=["dit", "ffn", "attention", "refblock", "refblock-shims",
+                                           "quant"],
                     default="dit")
     ap.add_argument("--attn-docs", default="32760,1024",
                     help="document lengths of the attention workload (comma-separated)")

@@ -209,44 +209,85 @@ class AttnBlock(_GemmTimer):
         per_row = self.hidden // 16           # scale bytes per weight row (blocked layout)
         return self.sf_qkv[r0 * per_row:r1 * per_row]
 
+    # K|V of a token-sharded block is projected, normed and all-gathered in
+    # this many head groups, each group's gather running on the side stream
+    # under the next group's projection and the previous group's attention
+    kv_groups = 2
+
+    def _kv_group_weights(self, G: int) -> list:
+        """Per head group g: the packed weight rows [K heads of g | V heads of
+        g] (2 * HD / G rows), their blocked scales (whole 128-row tiles, so a
+        row range is a contiguous byte range) and their global scales
+        [gs_k, gs_v], one per HD / G output columns.  Built once per G."""
+        cache = self.__dict__.setdefault("_kvg", {})
+        if G in cache:
+            return cache[G]
+        HD, per_row = self.inner, self.hidden // 16
+        hg = HD // G
+        groups = []
+        for g in range(G):
+            k0, v0 = HD + g * hg, 2 * HD + g * hg
+            w = torch.cat([self.w_qkv[k0:k0 + hg], self.w_qkv[v0:v0 + hg]]).contiguous()
+            sf = torch.cat([self.sf_qkv[k0 * per_row:(k0 + hg) * per_row],
+                            self.sf_qkv[v0 * per_row:(v0 + hg) * per_row]]).contiguous()
+            groups.append((w, sf, self.gs_qkv[1:3].contiguous()))
+        cache[G] = groups
+        return groups
+
+    def _groups_for(self, shard) -> int:
+        G = self.kv_groups
+        while G > 1 and (self.heads % G or (self.inner // G) % 128):
+            G -= 1
+        return G
+
     def _sharded_attention(self, qh, sfh, gsh, T, ws, dev, cos, sin, cu_seqlens, shard):
-        """Token-sharded attention: this rank's K|V rows (projection + key
-        norm/RoPE) go into its chunk of the full-sequence buffer and are
-        all-gathered on a side stream while the query projection and its
-        norm/RoPE run; one attention launch then covers every head.  Every
-        byte equals the unsharded run's (GEMM columns do not depend on the N
-        split; attention heads are independent)."""
+        """Token-sharded attention: for each head group, this rank's K|V rows
+        (projection + key norm/RoPE) go into its chunk of that group's
+        full-sequence buffer and are all-gathered on a side stream while the
+        main stream moves on (the next group's projection, the query
+        projection and norm/RoPE, then attention group by group, each waiting
+        only for its own gather).  Every byte equals the unsharded run's (GEMM
+        columns do not depend on the N split; heads are independent)."""
         HD, H, D = self.inner, self.heads, self.head_dim
+        G = self._groups_for(shard)
+        hg, Hg = HD // G, H // G
+        groups = self._kv_group_weights(G)
         q = _buf(ws, "q", (T, HD), torch.bfloat16, dev)
-        kv = _buf(ws, "kv", (shard.buffer_rows(), 2 * HD), torch.bfloat16, dev)
-        kv_local = kv[shard.row0:shard.row0 + T]
+        kvs = [_buf(ws, f"kv{g}", (shard.buffer_rows(), 2 * hg), torch.bfloat16, dev)
+               for g in range(G)]
         main = torch.cuda.current_stream(dev)
         side = ws.get("side")
         if side is None:
             side = ws["side"] = torch.cuda.Stream(device=dev)
+        gathered = []
         ev = self._event()
-        ops.gemm(qh, sfh, gsh, T, self.w_qkv[HD:], self._sf_rows(HD, 3 * HD), self.gs_qkv[1:],
-                 2 * HD, self.hidden, gsb_seg=HD, out=kv_local)
-        ops.qk_norm_rope(kv_local, H, D, q_off=0, k_off=0, wq=None, wk=self.norm_k,
-                         eps=self.qk_eps, cos=cos, sin=sin, heads_q=False)
-        ready = torch.cuda.Event()
-        ready.record(main)
-        side.wait_event(ready)
-        with torch.cuda.stream(side):
-            shard.all_gather(kv, kv_local)
-            gathered = torch.cuda.Event()
-            gathered.record(side)
+        for g, (w, sf, gs) in enumerate(groups):
+            kv_local = kvs[g][shard.row0:shard.row0 + T]
+            ops.gemm(qh, sfh, gsh, T, w, sf, gs, 2 * hg, self.hidden, gsb_seg=hg, out=kv_local)
+            ops.qk_norm_rope(kv_local, Hg, D, q_off=0, k_off=0, wq=None, wk=self.norm_k,
+                             eps=self.qk_eps, cos=cos, sin=sin, heads_q=False)
+            ready = torch.cuda.Event()
+            ready.record(main)
+            side.wait_event(ready)
+            with torch.cuda.stream(side):
+                shard.all_gather(kvs[g], kv_local)
+                done = torch.cuda.Event()
+                done.record(side)
+            gathered.append(done)
         ops.gemm(qh, sfh, gsh, T, self.w_qkv[:HD], self._sf_rows(0, HD), self.gs_qkv[:1], HD,
                  self.hidden, out=q)
         ops.qk_norm_rope(q, H, D, q_off=0, k_off=0, wq=self.norm_q, wk=None, eps=self.qk_eps,
                          cos=cos, sin=sin, heads_k=False)
         self._event(ev)
-        main.wait_event(gathered)        # also orders the next block's writes after the gather
-        ev = self._event(sink=self.attn_events)
-        o = ops.attention_varlen(q, H, D, cu_seqlens, q_off=0, k_off=0, v_off=HD,
-                                 kv=kv[:shard.total], q_row0=shard.row0,
-                                 out=_buf(ws, "o", (T, HD), torch.bfloat16, dev))
-        self._event(ev, sink=self.attn_events)
+        o = _buf(ws, "o", (T, HD), torch.bfloat16, dev)
+        for g in range(G):
+            # also orders the next block's writes to this group's buffer after the gather
+            main.wait_event(gathered[g])
+            ev = self._event(sink=self.attn_events)
+            ops.attention_varlen(q, Hg, D, cu_seqlens, q_off=g * hg, k_off=0, v_off=hg,
+                                 kv=kvs[g][:shard.total], q_row0=shard.row0,
+                                 out=o[:, g * hg:(g + 1) * hg])
+            self._event(ev, sink=self.attn_events)
         return o
 
     def __call__(self, x: torch.Tensor, rope: tuple[torch.Tensor, torch.Tensor] | None,

@@ -31,6 +31,7 @@ def run_bench(*args, env=None):
     ("quant", ["--cpu-rows", "16"], "GB/s"),
     ("attention", ["--cpu-rows", "16", "--attn-docs", "512,256"], "TFLOP/s"),
     ("refblock", ["--cpu-rows", "8"], "TFLOP/s"),
+    ("refblock-shims", ["--cpu-rows", "8"], "TFLOP/s"),
 ])
 def test_reference_arm_line(workload, extra, unit):
     lines = run_bench("--workload", workload, "--steps", "1", "--warmup", "0",

@@ -102,7 +102,12 @@ def test_sharded_attn_block_reproduces_unsharded(cuda):
     ws = blk._ws[("attn", T, d, HD, x.device, False)]
     amax_norm = ws["norm"]["amax"].clone()
     amax_o = ws["amax_o"].clone()
-    kv_ref = ws["qkv"][:, HD:].clone()
+    # the unsharded K|V per head group: [K heads of the group | V heads of it]
+    G = blk._groups_for(None)
+    hg = HD // G
+    kv_groups = [torch.cat([ws["qkv"][:, HD + g * hg:HD + (g + 1) * hg],
+                            ws["qkv"][:, 2 * HD + g * hg:2 * HD + (g + 1) * hg]], 1).clone()
+                 for g in range(G)]
     for a, b in [(0, 256), (256, 512)]:
         seen = []
 
@@ -115,12 +120,15 @@ def test_sharded_attn_block_reproduces_unsharded(cuda):
         calls = []
 
         def all_gather(kv, local):
-            calls.append(1)
-            assert torch.equal(local, kv_ref[a:b])        # local K|V after norm + RoPE
-            kv[:T].copy_(kv_ref)
+            # one call per head group, in order; the local K|V rows after
+            # norm + RoPE equal the unsharded run's
+            g = len(calls)
+            calls.append(g)
+            assert torch.equal(local, kv_groups[g][a:b])
+            kv[:T].copy_(kv_groups[g])
 
         shard = SequenceShard(a, b - a, T, all_gather, reduce_max)
         y = blk(x[a:b], (cos[a:b], sin[a:b]), cu, shard=shard)
         torch.cuda.synchronize()
-        assert calls == [1]
+        assert calls == list(range(G)) and G == 2
         assert torch.equal(y, full[a:b])
