@@ -116,3 +116,59 @@ def test_gemm_agrees_with_reference_scaled_mm(cuda):
     y = ops.gemm(qa, sfa, None, M, qb, sfb, None, N, K)
     torch.cuda.synchronize()
     assert R.max_rel_err(y.float().cpu().numpy(), ref.float().cpu().numpy()) <= 2e-3
+
+
+def test_pair_gemm_long_k_every_epilogue(cuda):
+    """K >= 8192 runs the CTA-pair kernel (one 256 x 256 tile per pair of SMs,
+    tcgen05 cta_group::2).  Ragged M = 300 puts the second pair's upper
+    128-row block wholly past the padded rows; every epilogue form is checked
+    against the oracle."""
+    M, N, K = 300, 768, 8192
+    x = seeded((M, K), seed=21)
+    w = seeded((N, K), seed=22, std=0.02)
+    bias = seeded((N,), seed=23, std=0.1)
+    res = seeded((M, N), seed=24)
+    gate = seeded((3, N), seed=25, std=0.5)
+    idx = torch.randint(0, 3, (M,), generator=torch.Generator().manual_seed(26), dtype=torch.int32)
+    qa, sfa, gsa = quant_dev(x, cuda)
+    qb, sfb, gsb = quant_dev(w, cuda)
+    base = oracle_gemm(qa, sfa, gsa, qb, sfb, gsb, M, N, K)
+
+    y = ops.gemm(qa, sfa, gsa, M, qb, sfb, gsb, N, K)
+    assert R.max_rel_err(y.float().cpu().numpy(), base) <= TOL
+
+    amax = torch.zeros(1, dtype=torch.float32, device=cuda)
+    y = ops.gemm(qa, sfa, gsa, M, qb, sfb, gsb, N, K, bias=bias.to(cuda), residual=res.to(cuda),
+                 act=ops.ACT_GELU_TANH, amax_out=amax)
+    got = y.float().cpu().numpy()
+    ref = R.gelu_tanh(base + bias.float().numpy()[None, :]) + res.float().numpy()
+    assert R.max_rel_err(got, ref) <= TOL
+    assert amax.item() == float(np.abs(got).max())
+
+    y = ops.gemm(qa, sfa, gsa, M, qb, sfb, gsb, N, K, residual=res.to(cuda), gate=gate.to(cuda),
+                 gate_idx=idx.to(cuda))
+    ref = base * gate.float().numpy()[idx.numpy()] + res.float().numpy()
+    assert R.max_rel_err(y.float().cpu().numpy(), ref) <= TOL
+
+    # three separately quantized weights of 256 rows, one GEMM
+    parts = [quant_dev(seeded((256, K), seed=27 + i, std=0.02 * (i + 1)), cuda) for i in range(3)]
+    y = ops.gemm(qa, sfa, gsa, M, torch.cat([p[0] for p in parts]), torch.cat([p[1] for p in parts]),
+                 torch.cat([p[2] for p in parts]), 768, K, gsb_seg=256)
+    for i, (q, s, g) in enumerate(parts):
+        ref = oracle_gemm(qa, sfa, gsa, q, s, g, M, 256, K)
+        assert R.max_rel_err(y[:, i * 256:(i + 1) * 256].float().cpu().numpy(), ref) <= TOL
+
+    # SwiGLU epilogue on a [value | gate] weight of 2F = 512 rows
+    F = 256
+    w2 = seeded((2 * F, K), seed=30, std=0.02)
+    perm = ops.swiglu_rows(F)
+    qw, sfw, gsw = quant_dev(w2[perm].contiguous(), cuda)
+    u = ops.gemm(qa, sfa, gsa, M, qw, sfw, gsw, 2 * F, K, act=ops.ACT_SWIGLU)
+    from oracle import blocks_ref as B
+    full = oracle_gemm(qa, sfa, gsa, qw, sfw, gsw, M, 2 * F, K)     # permuted column order
+    u2 = np.empty_like(full)
+    u2[:, perm.numpy()] = full
+    ref = R.bf16_round((R.bf16_round(u2[:, :F]) * B.silu_bf16(u2[:, F:])).astype(np.float32))
+    got = u.float().cpu().numpy()
+    assert np.isfinite(got).all()
+    assert R.max_rel_err(got, ref) <= TOL
