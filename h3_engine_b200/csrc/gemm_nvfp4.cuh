@@ -92,6 +92,123 @@ __device__ __forceinline__ float gelu_tanh(float v) {
   return 0.5f * v * (1.0f + t);
 }
 
+// The epilogue of one warp's 32 rows x 128 accumulator columns (columns
+// n0 + 128 * half ..) of a tile whose rows start at m0: alpha, bias, GELU or
+// SwiGLU, gate, residual, bf16, |D| max, staged in the warp's 4 KiB buffer and
+// written by TMA stores (rows >= M clipped).  Shared by the single-CTA and
+// the CTA-pair kernels.  Elementwise steps run as packed two-lane fp32 ops
+// (each lane the IEEE op the scalar form does); |D| max is kept on the bf16
+// bit patterns of |D| (non-negative bf16 values order like their 16-bit
+// integers), two per 32-bit word, and only when the caller asked for it.
+__device__ __forceinline__ void amax_bf16x2(uint32_t& amax2, uint32_t o) {
+  amax2 = __vmaxu2(amax2, o & 0x7FFF7FFFu);
+}
+__device__ __forceinline__ float amax_bf16x2_value(uint32_t amax2) {
+  return __uint_as_float(max(amax2 & 0xFFFFu, amax2 >> 16) << 16);
+}
+
+template <bool SWIGLU>
+__device__ __forceinline__ void epilogue_rows(const Args& p, const uint32_t (&acc)[128], int m0,
+                                              int n0, int half, int qd, int lane, uint8_t* stage,
+                                              uint32_t stage_s, float gsa, uint32_t& amax2) {
+  const int n_base = n0 + half * 128;
+  const bool want_amax = p.amax_out != nullptr;
+  if (SWIGLU) {
+    if (m0 + qd * 32 >= p.M) return;
+    const int row = m0 + qd * 32 + lane;
+    const bool row_ok = row < p.M;
+    const float alpha = gsa * (p.gs_b ? __ldg(p.gs_b) : 1.f);
+    if (lane == 0) bulk_wait_read0();
+    __syncwarp();
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      uint32_t o[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        float r[2];
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const float v = __bfloat162float(
+              __float2bfloat16_rn(__uint_as_float(acc[j * 8 + 2 * e + h]) * alpha));
+          const float g = __bfloat162float(
+              __float2bfloat16_rn(__uint_as_float(acc[64 + j * 8 + 2 * e + h]) * alpha));
+          const float sg = __bfloat162float(__float2bfloat16_rn(g / (1.0f + __expf(-g))));
+          r[h] = v * sg;
+        }
+        o[e] = pack_bf16x2(r[0], r[1]);
+        if (want_amax && row_ok) amax_bf16x2(amax2, o[e]);
+      }
+      *reinterpret_cast<uint4*>(stage + lane * 128 + ((j ^ (lane & 7)) << 4)) =
+          make_uint4(o[0], o[1], o[2], o[3]);
+    }
+    fence_proxy_async_smem();
+    __syncwarp();
+    if (lane == 0) {
+      tma_store_2d(&p.tmap_d, stage_s, (n0 >> 1) + half * 64, m0 + qd * 32);
+      bulk_commit();
+    }
+    return;
+  }
+  if (n_base >= p.N || m0 + qd * 32 >= p.M) return;   // warp-uniform
+  const int row = m0 + qd * 32 + lane;
+  const bool row_ok = row < p.M;
+  const float alpha = gsa * (p.gs_b ? __ldg(p.gs_b + (p.gsb_seg ? n_base / p.gsb_seg : 0)) : 1.f);
+  const float2 a2 = make_float2(alpha, alpha);
+#pragma unroll
+  for (int c = 0; c < 2; ++c) {
+    if (lane == 0) bulk_wait_read0();   // staging buffer free again
+    __syncwarp();
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int col = n_base + c * 64 + j * 8;
+      float2 v[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e)
+        v[e] = mul2(make_float2(__uint_as_float(acc[c * 64 + j * 8 + 2 * e]),
+                                __uint_as_float(acc[c * 64 + j * 8 + 2 * e + 1])), a2);
+      if (p.bias) {
+        const uint4 b = __ldg(reinterpret_cast<const uint4*>(p.bias + col));
+        const uint32_t bw[4] = {b.x, b.y, b.z, b.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) v[e] = add2(v[e], bf16x2_to_f2(bw[e]));
+      }
+      if (p.act == H3B_ACT_GELU_TANH) {
+#pragma unroll
+        for (int e = 0; e < 4; ++e) v[e] = make_float2(gelu_tanh(v[e].x), gelu_tanh(v[e].y));
+      }
+      if (p.gate) {
+        const long long grow = p.gate_idx ? (row_ok ? __ldg(p.gate_idx + row) : 0) : 0;
+        const uint4 b = __ldg(reinterpret_cast<const uint4*>(p.gate + grow * p.N + col));
+        const uint32_t bw[4] = {b.x, b.y, b.z, b.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) v[e] = mul2(v[e], bf16x2_to_f2(bw[e]));
+      }
+      if (p.residual && row_ok) {
+        const uint4 b =
+            __ldg(reinterpret_cast<const uint4*>(p.residual + (size_t)row * p.ldr + col));
+        const uint32_t bw[4] = {b.x, b.y, b.z, b.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) v[e] = add2(v[e], bf16x2_to_f2(bw[e]));
+      }
+      uint32_t o[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        o[e] = pack_bf16x2(v[e].x, v[e].y);
+        if (want_amax && row_ok) amax_bf16x2(amax2, o[e]);
+      }
+      // 128B swizzle: 16-byte chunk j of row `lane` sits at chunk j ^ (lane % 8)
+      *reinterpret_cast<uint4*>(stage + lane * 128 + ((j ^ (lane & 7)) << 4)) =
+          make_uint4(o[0], o[1], o[2], o[3]);
+    }
+    fence_proxy_async_smem();
+    __syncwarp();
+    if (lane == 0) {
+      tma_store_2d(&p.tmap_d, stage_s, n_base + c * OUT_CHUNK_COLS, m0 + qd * 32);
+      bulk_commit();
+    }
+  }
+}
+
 // SWIGLU: the fused up-projection epilogue (act == H3B_ACT_SWIGLU), a separate
 // instantiation so the other epilogues keep their register allocation.
 template <bool SWIGLU>
@@ -237,7 +354,7 @@ __global__ void __launch_bounds__(THREADS, 1) k_gemm_nvfp4(const __grid_constant
     uint8_t* stage = smem + OUT_OFFSET + ew * OUT_WARP_BYTES;
     const uint32_t stage_s = smem_u32(stage);
     const float gsa = p.gs_a ? __ldg(p.gs_a) : 1.f;
-    float amax = 0.f;
+    uint32_t amax2 = 0;                  // packed |bf16(D)| max of this warp's rows
     uint32_t i = 0;
     if (lane == 0) prefetch_tmap(&p.tmap_d);
     for (int t = blockIdx.x; t < p.num_tiles; t += gridDim.x, ++i) {
@@ -260,119 +377,11 @@ __global__ void __launch_bounds__(THREADS, 1) k_gemm_nvfp4(const __grid_constant
       __syncwarp();
       if (lane == 0) mbar_arrive(smem_u32(acc_empty));
 
-      const int n_base = n0 + half * 128;
-      if (SWIGLU) {
-       if (m0 + qd * 32 < p.M) {
-        // this warp's 128 accumulator columns are [value 64 | gate 64] of
-        // output columns n0/2 + 64*half ..; one 64-column chunk out
-        const int row = m0 + qd * 32 + lane;
-        const bool row_ok = row < p.M;
-        const float alpha = gsa * (p.gs_b ? __ldg(p.gs_b) : 1.f);
-        if (lane == 0) bulk_wait_read0();
-        __syncwarp();
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          uint32_t o[4];
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            float r[2];
-#pragma unroll
-            for (int h = 0; h < 2; ++h) {
-              const float v = __bfloat162float(
-                  __float2bfloat16_rn(__uint_as_float(acc[j * 8 + 2 * e + h]) * alpha));
-              const float g = __bfloat162float(
-                  __float2bfloat16_rn(__uint_as_float(acc[64 + j * 8 + 2 * e + h]) * alpha));
-              const float sg = __bfloat162float(__float2bfloat16_rn(g / (1.0f + __expf(-g))));
-              r[h] = v * sg;
-            }
-            o[e] = pack_bf16x2(r[0], r[1]);
-            if (row_ok) {
-              amax = fmaxf(amax, fabsf(__uint_as_float(o[e] << 16)));
-              amax = fmaxf(amax, fabsf(__uint_as_float(o[e] & 0xFFFF0000u)));
-            }
-          }
-          *reinterpret_cast<uint4*>(stage + lane * 128 + ((j ^ (lane & 7)) << 4)) =
-              make_uint4(o[0], o[1], o[2], o[3]);
-        }
-        fence_proxy_async_smem();
-        __syncwarp();
-        if (lane == 0) {
-          tma_store_2d(&p.tmap_d, stage_s, (n0 >> 1) + half * 64, m0 + qd * 32);
-          bulk_commit();
-        }
-       }
-      } else if (n_base < p.N && m0 + qd * 32 < p.M) {   // warp-uniform: this warp's box has rows
-        const int row = m0 + qd * 32 + lane;
-        const bool row_ok = row < p.M;
-        const float alpha =
-            gsa * (p.gs_b ? __ldg(p.gs_b + (p.gsb_seg ? n_base / p.gsb_seg : 0)) : 1.f);
-#pragma unroll
-        for (int c = 0; c < 2; ++c) {
-          if (lane == 0) bulk_wait_read0();   // staging buffer free again
-          __syncwarp();
-#pragma unroll
-          for (int j = 0; j < 8; ++j) {
-            const int col = n_base + c * 64 + j * 8;
-            float v[8];
-#pragma unroll
-            for (int e = 0; e < 8; ++e) v[e] = __uint_as_float(acc[c * 64 + j * 8 + e]) * alpha;
-            if (p.bias) {
-              const uint4 b = __ldg(reinterpret_cast<const uint4*>(p.bias + col));
-              const uint32_t bw[4] = {b.x, b.y, b.z, b.w};
-#pragma unroll
-              for (int e = 0; e < 4; ++e) {
-                v[2 * e] += __uint_as_float(bw[e] << 16);
-                v[2 * e + 1] += __uint_as_float(bw[e] & 0xFFFF0000u);
-              }
-            }
-            if (p.act == H3B_ACT_GELU_TANH) {
-#pragma unroll
-              for (int e = 0; e < 8; ++e) v[e] = gelu_tanh(v[e]);
-            }
-            if (p.gate) {
-              const long long grow = p.gate_idx ? (row_ok ? __ldg(p.gate_idx + row) : 0) : 0;
-              const uint4 b = __ldg(reinterpret_cast<const uint4*>(p.gate + grow * p.N + col));
-              const uint32_t bw[4] = {b.x, b.y, b.z, b.w};
-#pragma unroll
-              for (int e = 0; e < 4; ++e) {
-                v[2 * e] *= __uint_as_float(bw[e] << 16);
-                v[2 * e + 1] *= __uint_as_float(bw[e] & 0xFFFF0000u);
-              }
-            }
-            if (p.residual && row_ok) {
-              const uint4 b =
-                  __ldg(reinterpret_cast<const uint4*>(p.residual + (size_t)row * p.ldr + col));
-              const uint32_t bw[4] = {b.x, b.y, b.z, b.w};
-#pragma unroll
-              for (int e = 0; e < 4; ++e) {
-                v[2 * e] += __uint_as_float(bw[e] << 16);
-                v[2 * e + 1] += __uint_as_float(bw[e] & 0xFFFF0000u);
-              }
-            }
-            uint32_t o[4];
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              o[e] = pack_bf16x2(v[2 * e], v[2 * e + 1]);
-              if (row_ok) {
-                amax = fmaxf(amax, fabsf(__uint_as_float(o[e] << 16)));
-                amax = fmaxf(amax, fabsf(__uint_as_float(o[e] & 0xFFFF0000u)));
-              }
-            }
-            // 128B swizzle: 16-byte chunk j of row `lane` sits at chunk j ^ (lane % 8)
-            *reinterpret_cast<uint4*>(stage + lane * 128 + ((j ^ (lane & 7)) << 4)) =
-                make_uint4(o[0], o[1], o[2], o[3]);
-          }
-          fence_proxy_async_smem();
-          __syncwarp();
-          if (lane == 0) {
-            tma_store_2d(&p.tmap_d, stage_s, n_base + c * OUT_CHUNK_COLS, m0 + qd * 32);
-            bulk_commit();
-          }
-        }
-      }
+      epilogue_rows<SWIGLU>(p, acc, m0, n0, half, qd, lane, stage, stage_s, gsa, amax2);
     }
     if (lane == 0) bulk_wait0();
     if (p.amax_out) {
+      float amax = amax_bf16x2_value(amax2);
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
       if (lane == 0 && amax > 0.f)
@@ -386,124 +395,6 @@ __global__ void __launch_bounds__(THREADS, 1) k_gemm_nvfp4(const __grid_constant
     __syncwarp();
     tc_fence_after();
     tmem_dealloc(tmem, TMEM_COLS);
-  }
-}
-
-// The epilogue of one warp's 32 rows x 128 accumulator columns (columns
-// n0 + 128 * half ..) of a tile whose rows start at m0: alpha, bias, GELU or
-// SwiGLU, gate, residual, bf16, |D| max, staged in the warp's 4 KiB buffer and
-// written by TMA stores (rows >= M clipped).  The same steps as the
-// single-CTA kernel's epilogue, for the CTA-pair kernel.
-template <bool SWIGLU>
-__device__ __forceinline__ void epilogue_rows(const Args& p, const uint32_t (&acc)[128], int m0,
-                                              int n0, int half, int qd, int lane, uint8_t* stage,
-                                              uint32_t stage_s, float gsa, float& amax) {
-  const int n_base = n0 + half * 128;
-  if (SWIGLU) {
-    if (m0 + qd * 32 >= p.M) return;
-    const int row = m0 + qd * 32 + lane;
-    const bool row_ok = row < p.M;
-    const float alpha = gsa * (p.gs_b ? __ldg(p.gs_b) : 1.f);
-    if (lane == 0) bulk_wait_read0();
-    __syncwarp();
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      uint32_t o[4];
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        float r[2];
-#pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          const float v = __bfloat162float(
-              __float2bfloat16_rn(__uint_as_float(acc[j * 8 + 2 * e + h]) * alpha));
-          const float g = __bfloat162float(
-              __float2bfloat16_rn(__uint_as_float(acc[64 + j * 8 + 2 * e + h]) * alpha));
-          const float sg = __bfloat162float(__float2bfloat16_rn(g / (1.0f + __expf(-g))));
-          r[h] = v * sg;
-        }
-        o[e] = pack_bf16x2(r[0], r[1]);
-        if (row_ok) {
-          amax = fmaxf(amax, fabsf(__uint_as_float(o[e] << 16)));
-          amax = fmaxf(amax, fabsf(__uint_as_float(o[e] & 0xFFFF0000u)));
-        }
-      }
-      *reinterpret_cast<uint4*>(stage + lane * 128 + ((j ^ (lane & 7)) << 4)) =
-          make_uint4(o[0], o[1], o[2], o[3]);
-    }
-    fence_proxy_async_smem();
-    __syncwarp();
-    if (lane == 0) {
-      tma_store_2d(&p.tmap_d, stage_s, (n0 >> 1) + half * 64, m0 + qd * 32);
-      bulk_commit();
-    }
-    return;
-  }
-  if (n_base >= p.N || m0 + qd * 32 >= p.M) return;   // warp-uniform
-  const int row = m0 + qd * 32 + lane;
-  const bool row_ok = row < p.M;
-  const float alpha = gsa * (p.gs_b ? __ldg(p.gs_b + (p.gsb_seg ? n_base / p.gsb_seg : 0)) : 1.f);
-#pragma unroll
-  for (int c = 0; c < 2; ++c) {
-    if (lane == 0) bulk_wait_read0();   // staging buffer free again
-    __syncwarp();
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      const int col = n_base + c * 64 + j * 8;
-      float v[8];
-#pragma unroll
-      for (int e = 0; e < 8; ++e) v[e] = __uint_as_float(acc[c * 64 + j * 8 + e]) * alpha;
-      if (p.bias) {
-        const uint4 b = __ldg(reinterpret_cast<const uint4*>(p.bias + col));
-        const uint32_t bw[4] = {b.x, b.y, b.z, b.w};
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          v[2 * e] += __uint_as_float(bw[e] << 16);
-          v[2 * e + 1] += __uint_as_float(bw[e] & 0xFFFF0000u);
-        }
-      }
-      if (p.act == H3B_ACT_GELU_TANH) {
-#pragma unroll
-        for (int e = 0; e < 8; ++e) v[e] = gelu_tanh(v[e]);
-      }
-      if (p.gate) {
-        const long long grow = p.gate_idx ? (row_ok ? __ldg(p.gate_idx + row) : 0) : 0;
-        const uint4 b = __ldg(reinterpret_cast<const uint4*>(p.gate + grow * p.N + col));
-        const uint32_t bw[4] = {b.x, b.y, b.z, b.w};
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          v[2 * e] *= __uint_as_float(bw[e] << 16);
-          v[2 * e + 1] *= __uint_as_float(bw[e] & 0xFFFF0000u);
-        }
-      }
-      if (p.residual && row_ok) {
-        const uint4 b =
-            __ldg(reinterpret_cast<const uint4*>(p.residual + (size_t)row * p.ldr + col));
-        const uint32_t bw[4] = {b.x, b.y, b.z, b.w};
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          v[2 * e] += __uint_as_float(bw[e] << 16);
-          v[2 * e + 1] += __uint_as_float(bw[e] & 0xFFFF0000u);
-        }
-      }
-      uint32_t o[4];
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        o[e] = pack_bf16x2(v[2 * e], v[2 * e + 1]);
-        if (row_ok) {
-          amax = fmaxf(amax, fabsf(__uint_as_float(o[e] << 16)));
-          amax = fmaxf(amax, fabsf(__uint_as_float(o[e] & 0xFFFF0000u)));
-        }
-      }
-      // 128B swizzle: 16-byte chunk j of row `lane` sits at chunk j ^ (lane % 8)
-      *reinterpret_cast<uint4*>(stage + lane * 128 + ((j ^ (lane & 7)) << 4)) =
-          make_uint4(o[0], o[1], o[2], o[3]);
-    }
-    fence_proxy_async_smem();
-    __syncwarp();
-    if (lane == 0) {
-      tma_store_2d(&p.tmap_d, stage_s, n_base + c * OUT_CHUNK_COLS, m0 + qd * 32);
-      bulk_commit();
-    }
   }
 }
 
@@ -697,7 +588,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
     const uint32_t stage_s = smem_u32(stage);
     const uint32_t leader_acc_empty = mapa_shared(smem_u32(acc_empty), 0);
     const float gsa = p.gs_a ? __ldg(p.gs_a) : 1.f;
-    float amax = 0.f;
+    uint32_t amax2 = 0;                  // packed |bf16(D)| max of this warp's rows
     uint32_t i = 0;
     if (lane == 0) prefetch_tmap(&p.tmap_d);
     for (int t = pair_id; t < num_tiles; t += num_pairs, ++i) {
@@ -716,10 +607,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(leader_acc_empty);
-      epilogue_rows<SWIGLU>(p, acc, m0, n0, half, qd, lane, stage, stage_s, gsa, amax);
+      epilogue_rows<SWIGLU>(p, acc, m0, n0, half, qd, lane, stage, stage_s, gsa, amax2);
     }
     if (lane == 0) bulk_wait0();
     if (p.amax_out) {
+      float amax = amax_bf16x2_value(amax2);
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
       if (lane == 0 && amax > 0.f)
