@@ -178,6 +178,41 @@ class DiTWorkload:
         self.library_shapes = {"qkv": (M2, 3 * hd, d), "out": (M2, d, hd), "up": (M2, ff, d),
                                "down": (M2, d, ff), "square_8192": (8192, 8192, 8192)}
         self.config = self.describe(world)
+        # CUDA events around this rank's collectives (the K|V gather on its
+        # side stream, the amax max on the main stream), recorded only while
+        # the timers are set (the timed steps)
+        self._comm, self.comm_last = None, None
+        sh = self.sampler.shard
+        if sh is not None:
+            def timed(kind, fn):
+                def run(*a):
+                    ev = self._comm
+                    if ev is None:
+                        return fn(*a)
+                    st = torch.cuda.current_stream()
+                    e0 = torch.cuda.Event(enable_timing=True)
+                    e1 = torch.cuda.Event(enable_timing=True)
+                    e0.record(st)
+                    fn(*a)
+                    e1.record(st)
+                    ev.setdefault(kind, []).append((e0, e1))
+                return run
+            if sh.all_gather is not None:
+                sh.all_gather = timed("kv_gather", sh.all_gather)
+            sh.reduce_max = timed("amax_max", sh.reduce_max)
+
+    def comm_summary(self, steps: int) -> dict | None:
+        """Per timed step on this rank: calls and stream time of each
+        collective (a collective's time includes waiting for the other
+        ranks)."""
+        if not self.comm_last:
+            return None
+        out = {}
+        for kind, evs in self.comm_last.items():
+            tot = sum(a.elapsed_time(b) for a, b in evs)
+            out[kind] = {"calls_per_step": len(evs) / steps, "ms_per_step": tot / steps,
+                         "us_per_call": tot / max(len(evs), 1) * 1e3}
+        return out
 
     @staticmethod
     def describe(world: int) -> dict:
@@ -195,6 +230,10 @@ class DiTWorkload:
         for b in self.model.blocks:
             b.attn.gemm_events, b.ffn.gemm_events = gemm, gemm
             b.attn.attn_events = attn
+        if gemm is not None:
+            self._comm = {}
+        else:
+            self.comm_last, self._comm = self._comm, None
 
     def step(self):
         self.x = self.sampler.step(self.x, self.i % self.sampler.steps)
@@ -989,9 +1028,14 @@ def run_ours(args) -> None:
         }
         if wl.name == "dit":
             line["block_ms"] = ms / wl.cfg.blocks
+            comm = wl.comm_summary(args.steps)
+            if comm:
+                line["collectives_rank0"] = comm
         line.update(extras)
         print(json.dumps(line), flush=True)
     if world > 1:
+        if hasattr(wl, "layout"):
+            wl.layout.close()
         dist.barrier()
         dist.destroy_process_group()
 

@@ -57,6 +57,11 @@ SIGNATURES: dict[str, tuple] = {
                                             _c_void_p, _c_void_p, _c_void_p, _c_void_p,
                                             _c_void_p, _c_void_p, _i64, _c_void_p]),
     "h3b_selftest_bounded_wait": (_i32, [_i64, _c_void_p]),
+    "h3b_peer_buffer_create": (_i32, [_i64, ctypes.POINTER(_c_void_p), _c_void_p]),
+    "h3b_peer_buffer_open": (_i32, [_c_void_p, ctypes.POINTER(_c_void_p)]),
+    "h3b_peer_buffer_close": (_i32, [_c_void_p]),
+    "h3b_peer_buffer_destroy": (_i32, [_c_void_p]),
+    "h3b_amax_exchange": (_i32, [_c_void_p, _c_void_p, _i32, _i32, _i64, _i64, _c_void_p]),
 }
 
 _lock = threading.Lock()

@@ -21,6 +21,7 @@
 #include "rope.cuh"
 #include "attention.cuh"
 #include "elementwise.cuh"
+#include "peer.cuh"
 
 namespace h3b {
 
@@ -792,6 +793,62 @@ int h3b_selftest_bounded_wait(int64_t limit_us, void* stream) {
   if (rc != H3B_OK) return rc;
   k_selftest_bounded_wait<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(
       (uint64_t)limit_us * 1000ull);
+  return launched(cudaGetLastError());
+}
+
+// ------------------------------------------------------------------ peer amax exchange
+static_assert(sizeof(cudaIpcMemHandle_t) == H3B_PEER_HANDLE_BYTES, "IPC handle size");
+
+int h3b_peer_buffer_create(int64_t bytes, void** dev_ptr, void* ipc_handle) {
+  if (!dev_ptr || !ipc_handle || bytes <= 0 || bytes > (int64_t)(1 << 20))
+    return H3B_ERR_INVALID_ARG;
+  void* p = nullptr;
+  if (cudaMalloc(&p, (size_t)bytes) != cudaSuccess) return H3B_ERR_CUDA;
+  cudaIpcMemHandle_t h;
+  if (cudaMemset(p, 0, (size_t)bytes) != cudaSuccess || cudaDeviceSynchronize() != cudaSuccess ||
+      cudaIpcGetMemHandle(&h, p) != cudaSuccess) {
+    cudaFree(p);
+    return H3B_ERR_CUDA;
+  }
+  memcpy(ipc_handle, &h, sizeof(h));
+  *dev_ptr = p;
+  return H3B_OK;
+}
+
+int h3b_peer_buffer_open(const void* ipc_handle, void** dev_ptr) {
+  if (!ipc_handle || !dev_ptr) return H3B_ERR_INVALID_ARG;
+  cudaIpcMemHandle_t h;
+  memcpy(&h, ipc_handle, sizeof(h));
+  void* p = nullptr;
+  if (cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess)
+    return H3B_ERR_CUDA;
+  *dev_ptr = p;
+  return H3B_OK;
+}
+
+int h3b_peer_buffer_close(void* dev_ptr) {
+  if (!dev_ptr) return H3B_ERR_INVALID_ARG;
+  return cudaIpcCloseMemHandle(dev_ptr) == cudaSuccess ? H3B_OK : H3B_ERR_CUDA;
+}
+
+int h3b_peer_buffer_destroy(void* dev_ptr) {
+  if (!dev_ptr) return H3B_ERR_INVALID_ARG;
+  return cudaFree(dev_ptr) == cudaSuccess ? H3B_OK : H3B_ERR_CUDA;
+}
+
+int h3b_amax_exchange(float* amax, const void* slot_table, int rank, int world, int64_t epoch,
+                      int64_t limit_us, void* stream) {
+  if (!amax || !slot_table || world < 1 || world > peer::kMaxRanks || rank < 0 || rank >= world)
+    return H3B_ERR_INVALID_ARG;
+  if (epoch < 1 || epoch > (int64_t)0xFFFFFFFFll || limit_us < 1 || limit_us > 60000000)
+    return H3B_ERR_INVALID_ARG;
+  if ((reinterpret_cast<uintptr_t>(amax) & 3u) || (reinterpret_cast<uintptr_t>(slot_table) & 7u))
+    return H3B_ERR_ALIGNMENT;
+  int rc = check_sm100();
+  if (rc != H3B_OK) return rc;
+  peer::k_amax_exchange<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(
+      amax, static_cast<const unsigned long long* const*>(slot_table), rank, world,
+      (uint32_t)epoch, (uint64_t)limit_us * 1000ull);
   return launched(cudaGetLastError());
 }
 

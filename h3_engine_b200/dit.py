@@ -24,6 +24,7 @@ import math
 from dataclasses import dataclass
 
 import torch
+import torch.distributed as dist
 
 from . import ops
 from .blocks import AttnBlock, DiTBlock, FFNBlock
@@ -193,6 +194,11 @@ class Sampler:
         row0, rows, _ = layout.shard_rows(T)
         self.rows = slice(row0, row0 + rows)
         self.shard = layout.sequence_shard(T)
+        if layout.peer_amax is not None:
+            # every rank has its model before the first device-side amax
+            # exchange, whose wait for the other ranks is bounded
+            torch.cuda.synchronize()
+            dist.barrier()
 
     def step(self, x: torch.Tensor, i: int) -> torch.Tensor:
         """One denoising step on this rank's latent rows ``x`` [rows, d]."""

@@ -8,9 +8,12 @@ Every GEMM, quantization and norm is row-independent, so token shards only
 meet in attention: after qk-norm + RoPE each rank writes its K|V rows into its
 chunk of a full-sequence buffer and one in-place all-gather over the token
 group completes it (the only bulk exchange per block).  Every NVFP4
-quantization first max-all-reduces its 4-byte amax over all ranks, so each
+quantization first takes the max of its 4-byte amax over all ranks, so each
 activation of the CFG batch keeps one global scale and every layout computes
-the same bytes as the single-GPU run.  The CFG combine exchanges each rank's
+the same bytes as the single-GPU run.  On NCCL runs that max goes through
+peer memory (``PeerAmax``: one warp stores this rank's value into every
+peer's slot array and polls its own, a bounded device-side wait, no host
+collective); elsewhere (gloo) through an all-reduce.  The CFG combine exchanges each rank's
 velocity rows with its peer in the other branch once per step.
 
 ``split_rows`` / ``ParallelLayout`` are pure host logic (tested on CPU with
@@ -36,6 +39,92 @@ def split_rows(total: int, parts: int, index: int) -> tuple[int, int, int]:
     return row0, rows, chunk
 
 
+class PeerMemoryUnavailable(RuntimeError):
+    """Peer memory could not be set up on some rank (no CUDA IPC / peer access)."""
+
+
+class PeerAmax:
+    """The max of a 4-byte fp32 amax over all ranks through peer memory.
+
+    Each rank allocates a zeroed slot array of 2 * world 64-bit words
+    (``h3b_peer_buffer_create``), the ranks swap its CUDA IPC handle once
+    (``all_gather_object``) and map each other's (``h3b_peer_buffer_open``).
+    Exchange number e (counted identically on every rank, because every rank
+    quantizes the same activations in the same order) is one
+    ``h3b_amax_exchange`` launch on the current stream: no NCCL kernel and no
+    host synchronization per quantization.  A rank that never arrives makes
+    the others' wait expire after ``limit_us`` with H3B_ERR_TIMEOUT recorded
+    in the device error word (their amax stays local).  Every rank must call
+    ``close`` (a collective) before the process group is destroyed."""
+
+    def __init__(self, rank: int, world: int, device: torch.device, group=None,
+                 limit_us: int = 30_000_000):
+        """Collective over ``group``.  Raises ``PeerMemoryUnavailable`` on
+        every rank, after undoing its own set-up, if any rank could not
+        allocate, export or map a slot array."""
+        import ctypes
+        from . import _lib
+        self.rank, self.world, self.limit_us, self.group = rank, world, limit_us, group
+        lib = _lib.lib()
+        handle = (ctypes.c_uint8 * 64)()
+        own = ctypes.c_void_p()
+        with torch.cuda.device(device):
+            made = lib.h3b_peer_buffer_create(2 * world * 8, ctypes.byref(own), handle) == 0
+        handles: list = [None] * world
+        dist.all_gather_object(handles, bytes(handle) if made else None, group=group)
+        ptrs, self._opened = [], []
+        ok = all(h is not None for h in handles)
+        with torch.cuda.device(device):
+            for r in range(world):
+                if not ok:
+                    break
+                if r == rank:
+                    ptrs.append(own.value)
+                    continue
+                buf = (ctypes.c_uint8 * 64).from_buffer_copy(handles[r])
+                p = ctypes.c_void_p()
+                if lib.h3b_peer_buffer_open(buf, ctypes.byref(p)) != 0:
+                    ok = False
+                    break
+                ptrs.append(p.value)
+                self._opened.append(p.value)
+        # every rank learns whether every rank is mapped
+        flags: list = [None] * world
+        dist.all_gather_object(flags, ok, group=group)
+        self._own = own.value if made else None
+        if not all(flags):
+            self._release(lib)
+            raise PeerMemoryUnavailable("a rank could not allocate, export or map its slot array")
+        self.table = torch.tensor(ptrs, dtype=torch.int64, device=device)
+        self.epoch = 0
+
+    def _release(self, lib) -> None:
+        import ctypes
+        from . import _lib
+        for p in self._opened:
+            _lib.check(lib.h3b_peer_buffer_close(ctypes.c_void_p(p)), "h3b_peer_buffer_close")
+        if self._own is not None:
+            _lib.check(lib.h3b_peer_buffer_destroy(ctypes.c_void_p(self._own)),
+                       "h3b_peer_buffer_destroy")
+        self._own, self._opened = None, []
+
+    def __call__(self, t: torch.Tensor) -> None:
+        from . import torch_ops  # noqa: F401  (registers torch.ops.h3b)
+        self.epoch += 1
+        torch.ops.h3b.amax_exchange(t, self.table, self.rank, self.world, self.epoch,
+                                    self.limit_us)
+
+    def close(self) -> None:
+        """Unmap the peers' arrays and free this rank's, after every rank's
+        last exchange (a barrier over the group)."""
+        from . import _lib
+        if self._own is None:
+            return
+        torch.cuda.synchronize()
+        dist.barrier(group=self.group)
+        self._release(_lib.lib())
+
+
 @dataclass
 class ParallelLayout:
     world: int
@@ -46,6 +135,7 @@ class ParallelLayout:
     token_rank: int
     token_group: object = None   # process group of this rank's token shards
     pair_group: object = None    # {this rank, its peer in the other branch}
+    peer_amax: object = None     # PeerAmax over all ranks (NCCL runs)
 
     @staticmethod
     def plan(world: int, rank: int) -> "ParallelLayout":
@@ -74,6 +164,24 @@ class ParallelLayout:
             g = dist.new_group(ranks)
             if t == self.token_rank:
                 self.pair_group = g
+        # the amax max through peer memory on NCCL (GPU) runs;
+        # H3B_AMAX_VIA=nccl keeps the NCCL all-reduce
+        if dist.get_backend() == "nccl" and os.environ.get("H3B_AMAX_VIA", "peer") == "peer":
+            dev = torch.device("cuda", torch.cuda.current_device())
+            try:
+                self.peer_amax = PeerAmax(self.rank, self.world, dev)
+            except PeerMemoryUnavailable as e:
+                # decided on every rank alike: the NCCL all-reduce instead
+                import warnings
+                warnings.warn(f"amax exchange through NCCL: {e}")
+                self.peer_amax = None
+
+    def close(self) -> None:
+        """Release the peer-memory amax exchange (a collective: every rank,
+        after its last step, before the process group is destroyed)."""
+        if self.peer_amax is not None:
+            self.peer_amax.close()
+            self.peer_amax = None
 
     def sequence_shard(self, total: int) -> SequenceShard | None:
         """None on one GPU; otherwise this rank's shard with the K|V gather over
@@ -96,6 +204,9 @@ class ParallelLayout:
 
         def reduce_max(t: torch.Tensor) -> None:
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
+
+        if self.peer_amax is not None:
+            reduce_max = self.peer_amax  # noqa: F811
 
         gather = all_gather if self.token_parallel > 1 else None
         return SequenceShard(row0, rows, total, gather, reduce_max, chunk=chunk,

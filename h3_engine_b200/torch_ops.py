@@ -178,3 +178,11 @@ def ada_modulate(x: torch.Tensor, ldx: int, scale: torch.Tensor, shift: torch.Te
     """out = x * (1 + scale[idx]) + shift[idx], torch's bf16 rounding (h3b_ada_modulate)."""
     _run(out, "h3b_ada_modulate", _p(x), ldx, _p(scale), _p(shift), _p(idx), n_idx, rows, cols,
          _p(out), ldo)
+
+
+@_op("amax_exchange", ("amax",))
+def amax_exchange(amax: torch.Tensor, slot_table: torch.Tensor, rank: int, world: int,
+                  epoch: int, limit_us: int) -> None:
+    """amax[0] = max over the ranks of each rank's amax[0], through peer
+    memory (h3b_amax_exchange); slot_table: int64 [world] device pointers."""
+    _run(amax, "h3b_amax_exchange", _p(amax), _p(slot_table), rank, world, epoch, limit_us)

@@ -256,6 +256,37 @@ H3B_API int h3b_rmsnorm_quantize_noalloc(const void* x, int64_t M, int64_t K, in
  * h3b_device_error.  1 <= limit_us <= 1000000, else H3B_ERR_INVALID_ARG.    */
 H3B_API int h3b_selftest_bounded_wait(int64_t limit_us, void* stream);
 
+/* ------------------------------------------------------------------ peer amax exchange
+ * The max of a per-rank fp32 amax over the ranks of a sharded run, through
+ * peer memory (replaces the NCCL max all-reduce before every NVFP4
+ * activation quantization of a token-/CFG-sharded run, which keeps one
+ * global scale per activation as QuantizedActivation computes it over the
+ * whole tensor, h3_inference/nvfp4.py:92-110).
+ *
+ * Set-up, once per run on every rank (not on the hot path):
+ *   h3b_peer_buffer_create  cudaMalloc'd, zeroed slot array of `bytes`
+ *                           (2 * world * 8 bytes) on the current device and
+ *                           its CUDA IPC handle (H3B_PEER_HANDLE_BYTES bytes)
+ *   h3b_peer_buffer_open    maps another rank's array from its handle
+ *   h3b_peer_buffer_close / h3b_peer_buffer_destroy  undo the two
+ * Exchange number `epoch` (1, 2, 3, ... in the same order on every rank):
+ *   h3b_amax_exchange       *amax = max over ranks of each rank's *amax;
+ *                           slot_table: device array of `world` pointers,
+ *                           entry r = rank r's array as mapped here (entry
+ *                           `rank` = this rank's own).  One warp; peer stores
+ *                           and polling loads, no multicast.  The wait for the
+ *                           other ranks is bounded by limit_us (1 ..
+ *                           60000000): on expiry the kernel records
+ *                           H3B_ERR_TIMEOUT, leaves *amax local and returns.
+ * world <= 32.                                                             */
+#define H3B_PEER_HANDLE_BYTES 64
+H3B_API int h3b_peer_buffer_create(int64_t bytes, void** dev_ptr, void* ipc_handle);
+H3B_API int h3b_peer_buffer_open(const void* ipc_handle, void** dev_ptr);
+H3B_API int h3b_peer_buffer_close(void* dev_ptr);
+H3B_API int h3b_peer_buffer_destroy(void* dev_ptr);
+H3B_API int h3b_amax_exchange(float* amax, const void* slot_table, int rank, int world,
+                              int64_t epoch, int64_t limit_us, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

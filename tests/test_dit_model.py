@@ -152,35 +152,44 @@ def _port():
     return p
 
 
-def _layout_worker(rank, world, port, q):
+def _layout_worker(rank, world, port, q, amax_via="peer"):
     import torch.distributed as dist
     from datetime import timedelta
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank),
-                      WORLD_SIZE=str(world), LOCAL_RANK=str(rank))
+                      WORLD_SIZE=str(world), LOCAL_RANK=str(rank), H3B_AMAX_VIA=amax_via)
     dev = torch.device("cuda", rank)
     torch.cuda.set_device(dev)
     dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev,
                             timeout=timedelta(seconds=60))
+    L = None
     try:
+        from h3_engine_b200 import _lib
         from h3_engine_b200.dit import RandomDiT, Sampler
         from h3_engine_b200.parallel import ParallelLayout
         L = ParallelLayout.plan(world, rank)
         L.build_groups()
+        assert (L.peer_amax is not None) == (amax_via == "peer")
         model = RandomDiT(tiny_cfg(), dev, seed=4)
         sampler = Sampler(model, L, steps=8)
         x1 = sampler.step(sampler.latent(), 0)
         torch.cuda.synchronize()
-        q.put((rank, sampler.rows.start, x1.cpu()))
+        err = _lib.device_error()      # a peer wait that expired would show here
+        q.put((rank, sampler.rows.start if err == 0 else -1,
+               x1.cpu() if err == 0 else f"device error {err}"))
     except Exception as e:   # pragma: no cover
         q.put((rank, -1, repr(e)))
     finally:
+        if L is not None:
+            L.close()
         dist.barrier()
         dist.destroy_process_group()
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-@pytest.mark.parametrize("world", [2, 4, 8])
-def test_distributed_layouts_match_single_gpu(cuda, world):
+@pytest.mark.parametrize("world,amax_via", [(2, "peer"), (4, "peer"), (8, "peer"), (2, "nccl")])
+def test_distributed_layouts_match_single_gpu(cuda, world, amax_via):
+    """Every layout computes the 1-GPU bytes, with the amax max through peer
+    memory (the default on NCCL runs) and through the NCCL all-reduce."""
     if torch.cuda.device_count() < world:
         pytest.skip(f"needs {world} GPUs")
     import torch.multiprocessing as mp
@@ -192,7 +201,8 @@ def test_distributed_layouts_match_single_gpu(cuda, world):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _port()
-    procs = [ctx.Process(target=_layout_worker, args=(r, world, port, q)) for r in range(world)]
+    procs = [ctx.Process(target=_layout_worker, args=(r, world, port, q, amax_via))
+             for r in range(world)]
     for p in procs:
         p.start()
     res = [q.get(timeout=300) for _ in procs]

@@ -26,6 +26,7 @@ OPS = {
     "attention_qkv": {"out"},
     "gate_residual": {"out"},
     "ada_modulate": {"out"},
+    "amax_exchange": {"amax"},
 }
 
 
