@@ -91,6 +91,16 @@ __device__ __forceinline__ float gelu_tanh(float v) {
   asm("tanh.approx.f32 %0, %1;" : "=f"(t) : "f"(u));
   return 0.5f * v * (1.0f + t);
 }
+// The same for two lanes with packed fp32 ops (each lane the scalar op above,
+// in the same order: the same bits).
+__device__ __forceinline__ float2 gelu_tanh2(float2 v) {
+  const float2 inner = fma2(mul2(make_float2(0.044715f, 0.044715f), v), mul2(v, v), v);
+  const float2 u = mul2(make_float2(0.7978845608028654f, 0.7978845608028654f), inner);
+  float2 t;
+  asm("tanh.approx.f32 %0, %1;" : "=f"(t.x) : "f"(u.x));
+  asm("tanh.approx.f32 %0, %1;" : "=f"(t.y) : "f"(u.y));
+  return mul2(mul2(make_float2(0.5f, 0.5f), v), add2(make_float2(1.0f, 1.0f), t));
+}
 
 // The epilogue of one warp's 32 rows x 128 accumulator columns (columns
 // n0 + 128 * half ..) of a tile whose rows start at m0: alpha, bias, GELU or
@@ -174,7 +184,7 @@ __device__ __forceinline__ void epilogue_rows(const Args& p, const uint32_t (&ac
       }
       if (p.act == H3B_ACT_GELU_TANH) {
 #pragma unroll
-        for (int e = 0; e < 4; ++e) v[e] = make_float2(gelu_tanh(v[e].x), gelu_tanh(v[e].y));
+        for (int e = 0; e < 4; ++e) v[e] = gelu_tanh2(v[e]);
       }
       if (p.gate) {
         const long long grow = p.gate_idx ? (row_ok ? __ldg(p.gate_idx + row) : 0) : 0;
