@@ -27,6 +27,7 @@ from dataclasses import dataclass
 import torch
 import torch.distributed as dist
 
+from . import torch_ops  # noqa: F401  (registers torch.ops.h3b)
 from .blocks import SequenceShard
 
 
@@ -109,7 +110,6 @@ class PeerAmax:
         self._own, self._opened = None, []
 
     def __call__(self, t: torch.Tensor) -> None:
-        from . import torch_ops  # noqa: F401  (registers torch.ops.h3b)
         self.epoch += 1
         torch.ops.h3b.amax_exchange(t, self.table, self.rank, self.world, self.epoch,
                                     self.limit_us)
