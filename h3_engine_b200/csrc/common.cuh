@@ -290,23 +290,25 @@ __device__ __forceinline__ void tc_mma_bf16_ts_elect(uint32_t d_tmem, uint32_t a
       "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(0u)
       : "memory");
 }
-__device__ __forceinline__ void tc_mma_nvf4_elect(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
-                                                  uint32_t idesc, uint32_t sfa_tmem, uint32_t sfb_tmem,
-                                                  uint32_t accumulate) {
+// One MMA k-step of the block-scaled GEMM under a single elected lane: the
+// three scale copies it reads (A's 128 rows, B's two 128-row halves) and the
+// MMA, issued back to back (tcgen05 ops of one thread execute in order).
+__device__ __forceinline__ void tc_kstep_nvf4_elect(uint32_t sfa_t, uint64_t sfa_d, uint32_t sfb_t0,
+                                                    uint64_t sfb_d0, uint32_t sfb_t1,
+                                                    uint64_t sfb_d1, uint32_t d_tmem,
+                                                    uint64_t a_desc, uint64_t b_desc,
+                                                    uint32_t idesc, uint32_t accumulate) {
   asm volatile(
       "{\n\t.reg .pred p, e;\n\t"
-      "setp.ne.b32 p, %6, 0;\n\t"
+      "setp.ne.b32 p, %10, 0;\n\t"
       "elect.sync _|e, 0xffffffff;\n\t"
+      "@e tcgen05.cp.cta_group::1.32x128b.warpx4 [%0], %1;\n\t"
+      "@e tcgen05.cp.cta_group::1.32x128b.warpx4 [%2], %3;\n\t"
+      "@e tcgen05.cp.cta_group::1.32x128b.warpx4 [%4], %5;\n\t"
       "@e tcgen05.mma.cta_group::1.kind::mxf4nvf4.block_scale.scale_vec::4X"
-      " [%0], %1, %2, %3, [%4], [%5], p;\n\t}" ::"r"(d_tmem),
-      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(sfa_tmem), "r"(sfb_tmem), "r"(accumulate)
-      : "memory");
-}
-__device__ __forceinline__ void tc_cp_32x128b_warpx4_elect(uint32_t taddr, uint64_t sdesc) {
-  asm volatile(
-      "{\n\t.reg .pred e;\n\t"
-      "elect.sync _|e, 0xffffffff;\n\t"
-      "@e tcgen05.cp.cta_group::1.32x128b.warpx4 [%0], %1;\n\t}" ::"r"(taddr), "l"(sdesc)
+      " [%6], %7, %8, %9, [%0], [%2], p;\n\t}" ::"r"(sfa_t),
+      "l"(sfa_d), "r"(sfb_t0), "l"(sfb_d0), "r"(sfb_t1), "l"(sfb_d1), "r"(d_tmem), "l"(a_desc),
+      "l"(b_desc), "r"(idesc), "r"(accumulate)
       : "memory");
 }
 
@@ -441,29 +443,25 @@ __device__ __forceinline__ void tc_commit_pair_elect(uint32_t bar, uint16_t cta_
       "h"(cta_mask)
       : "memory");
 }
-// Scale atoms -> tensor memory in both CTAs of the pair, each from its own
-// shared memory at the same offset.
-__device__ __forceinline__ void tc_cp_32x128b_warpx4_pair_elect(uint32_t taddr, uint64_t sdesc) {
-  asm volatile(
-      "{\n\t.reg .pred e;\n\t"
-      "elect.sync _|e, 0xffffffff;\n\t"
-      "@e tcgen05.cp.cta_group::2.32x128b.warpx4 [%0], %1;\n\t}" ::"r"(taddr), "l"(sdesc)
-      : "memory");
-}
-// The pair MMA: D (M=256 over the two CTAs' tensor memory) (+)= (A * sfA) x
-// (B * sfB)^T; A rows and B columns split between the CTAs' shared memory at
-// the same offsets.
-__device__ __forceinline__ void tc_mma_nvf4_pair_elect(uint32_t d_tmem, uint64_t a_desc,
-                                                       uint64_t b_desc, uint32_t idesc,
-                                                       uint32_t sfa_tmem, uint32_t sfb_tmem,
-                                                       uint32_t accumulate) {
+// One k-step of the pair GEMM under a single elected lane of the leader: the
+// three pair scale copies and the pair MMA, back to back.
+__device__ __forceinline__ void tc_kstep_nvf4_pair_elect(uint32_t sfa_t, uint64_t sfa_d,
+                                                         uint32_t sfb_t0, uint64_t sfb_d0,
+                                                         uint32_t sfb_t1, uint64_t sfb_d1,
+                                                         uint32_t d_tmem, uint64_t a_desc,
+                                                         uint64_t b_desc, uint32_t idesc,
+                                                         uint32_t accumulate) {
   asm volatile(
       "{\n\t.reg .pred p, e;\n\t"
-      "setp.ne.b32 p, %6, 0;\n\t"
+      "setp.ne.b32 p, %10, 0;\n\t"
       "elect.sync _|e, 0xffffffff;\n\t"
+      "@e tcgen05.cp.cta_group::2.32x128b.warpx4 [%0], %1;\n\t"
+      "@e tcgen05.cp.cta_group::2.32x128b.warpx4 [%2], %3;\n\t"
+      "@e tcgen05.cp.cta_group::2.32x128b.warpx4 [%4], %5;\n\t"
       "@e tcgen05.mma.cta_group::2.kind::mxf4nvf4.block_scale.scale_vec::4X"
-      " [%0], %1, %2, %3, [%4], [%5], p;\n\t}" ::"r"(d_tmem),
-      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(sfa_tmem), "r"(sfb_tmem), "r"(accumulate)
+      " [%6], %7, %8, %9, [%0], [%2], p;\n\t}" ::"r"(sfa_t),
+      "l"(sfa_d), "r"(sfb_t0), "l"(sfb_d0), "r"(sfb_t1), "l"(sfb_d1), "r"(d_tmem), "l"(a_desc),
+      "l"(b_desc), "r"(idesc), "r"(accumulate)
       : "memory");
 }
 

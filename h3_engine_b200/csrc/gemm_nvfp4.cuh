@@ -303,10 +303,12 @@ __global__ void __launch_bounds__(THREADS, 1) k_gemm_nvfp4(const __grid_constant
       }
     }
   } else if (warp == 1) {
-    // The whole warp runs the issue loop on warp-uniform values; one elected
-    // lane issues each tcgen05 op (a converged issuer keeps pace beside the
-    // busy epilogue warps).  Descriptors advance by adding (offset >> 4) to
-    // the start-address field.
+    // The whole warp runs the issue loop on warp-uniform values; per MMA
+    // k-step one elected lane issues the three scale copies and the MMA back
+    // to back (a converged issuer keeps pace beside the busy epilogue warps,
+    // and one election per k-step instead of one per op takes the issue
+    // stream, the kernel's limit, from ~40 cycles per op down).  Descriptors
+    // advance by adding (offset >> 4) to the start-address field.
     auto wait = [&](uint64_t* bar, uint32_t parity) -> bool {
       return __all_sync(0xffffffffu, mbar_wait(smem_u32(bar), parity, abort_flag));
     };
@@ -331,18 +333,15 @@ __global__ void __launch_bounds__(THREADS, 1) k_gemm_nvfp4(const __grid_constant
         const uint32_t sf_t = tmem + SF_COL + s * SF_STAGE_COLS;
         const uint64_t sfa_d = desc_sf_atom(smem_u32(sSFA(s)));
         const uint64_t sfb_d = desc_sf_atom(smem_u32(sSFB(s)));
-#pragma unroll
-        for (int kk = 0; kk < 4; ++kk) {
-          tc_cp_32x128b_warpx4_elect(sf_t + kk * 4, sfa_d + ((kk * SF_ATOM) >> 4));
-          tc_cp_32x128b_warpx4_elect(sf_t + 16 + kk * 8, sfb_d + ((kk * SF_ATOM) >> 4));
-          tc_cp_32x128b_warpx4_elect(sf_t + 16 + kk * 8 + 4, sfb_d + (((4 + kk) * SF_ATOM) >> 4));
-        }
         const uint64_t a_d = desc_kmajor_sw128(smem_u32(sA(s)));
         const uint64_t b_d = desc_kmajor_sw128(smem_u32(sB(s)));
 #pragma unroll
         for (int kk = 0; kk < 4; ++kk) {
-          tc_mma_nvf4_elect(tmem + ACC_COL, a_d + ((kk * 32) >> 4), b_d + ((kk * 32) >> 4), IDESC,
-                            sf_t + kk * 4, sf_t + 16 + kk * 8, (kb | kk) != 0);
+          tc_kstep_nvf4_elect(sf_t + kk * 4, sfa_d + ((kk * SF_ATOM) >> 4), sf_t + 16 + kk * 8,
+                              sfb_d + ((kk * SF_ATOM) >> 4), sf_t + 16 + kk * 8 + 4,
+                              sfb_d + (((4 + kk) * SF_ATOM) >> 4), tmem + ACC_COL,
+                              a_d + ((kk * 32) >> 4), b_d + ((kk * 32) >> 4), IDESC,
+                              (kb | kk) != 0);
         }
         tc_commit_elect(smem_u32(&empty[s]));
       }
@@ -565,19 +564,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
           const uint32_t sf_t = tmem + SF_COL + s * SF_STAGE_COLS;
           const uint64_t sfa_d = desc_sf_atom(smem_u32(sSFA(s)));
           const uint64_t sfb_d = desc_sf_atom(smem_u32(sSFB(s)));
-#pragma unroll
-          for (int kk = 0; kk < 4; ++kk) {
-            tc_cp_32x128b_warpx4_pair_elect(sf_t + kk * 4, sfa_d + ((kk * SF_ATOM) >> 4));
-            tc_cp_32x128b_warpx4_pair_elect(sf_t + 16 + kk * 8, sfb_d + ((kk * SF_ATOM) >> 4));
-            tc_cp_32x128b_warpx4_pair_elect(sf_t + 16 + kk * 8 + 4,
-                                            sfb_d + (((4 + kk) * SF_ATOM) >> 4));
-          }
           const uint64_t a_d = desc_kmajor_sw128(smem_u32(sA(s)));
           const uint64_t b_d = desc_kmajor_sw128(smem_u32(sB(s)));
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk) {
-            tc_mma_nvf4_pair_elect(tmem + ACC_COL, a_d + ((kk * 32) >> 4), b_d + ((kk * 32) >> 4),
-                                   P_IDESC, sf_t + kk * 4, sf_t + 16 + kk * 8, (kb | kk) != 0);
+            tc_kstep_nvf4_pair_elect(sf_t + kk * 4, sfa_d + ((kk * SF_ATOM) >> 4),
+                                     sf_t + 16 + kk * 8, sfb_d + ((kk * SF_ATOM) >> 4),
+                                     sf_t + 16 + kk * 8 + 4, sfb_d + (((4 + kk) * SF_ATOM) >> 4),
+                                     tmem + ACC_COL, a_d + ((kk * 32) >> 4),
+                                     b_d + ((kk * 32) >> 4), P_IDESC, (kb | kk) != 0);
           }
           tc_commit_pair_elect(smem_u32(&empty[s]), 0x3);
         }
