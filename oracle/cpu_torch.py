@@ -1,5 +1,5 @@
 """Multi-threaded torch-CPU port of the NVFP4 recipe and the FFN sub-block --
-TEST / BASELINE INFRASTRUCTURE ONLY.
+TEST / CPU-BASELINE INFRASTRUCTURE ONLY.
 
 This is the timed CPU baseline (``bench.py --impl reference`` and the
 ``cpu_baseline`` object): the reference's NVFP4 path cannot run on a CPU
